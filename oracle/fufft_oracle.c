@@ -1,0 +1,672 @@
+/*
+ * fufft_oracle.c -- TEST INFRASTRUCTURE ONLY.
+ *
+ * A plain-C restatement of the CPU transcription that weiwang217/FuFFT uses as
+ * its own oracle (verify_kernel.cpp).  It is the checker for the sm_100a
+ * kernels of fufft_b200 and is never linked into, called by, or shipped with
+ * the product library.  Only tests/, __graft_entry__.smoke() and bench.py's
+ * cpu_baseline leg load it.
+ *
+ * The arithmetic follows the reference operation by operation (same fmaf
+ * complex multiply, same specialised x(+-i) / x w^1 / x w^3 forms, same
+ * twiddle recurrences with cosf/sinf), so for identical fp32 inputs it
+ * reproduces the reference transcription bit for bit.  That claim is pinned by
+ * tests/test_oracle_golden.py against fixtures generated from the reference's
+ * own code (tests/golden/make_golden.py, oracle/ref_harness.cpp).
+ *
+ * The shared-memory swizzles of the reference (SWZ, SWZ16) are bijections that
+ * are applied to every access, so they do not change any value; this oracle
+ * works on the logical (unswizzled) arrays.  The slot/lane/CPB loops of the
+ * reference only enumerate disjoint butterfly groups, so their order does not
+ * change any value either; here the groups run in index order.
+ *
+ * Build: see oracle/Makefile (gcc -O2 -ffp-contract=off -fPIC -shared).
+ * -ffp-contract=off matters: the reference's products and sums round
+ * separately except where it calls fmaf explicitly.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+typedef struct { float re, im; } cpx;
+typedef struct { double re, im; } cpxd;
+
+#define ORC_2PI_F 6.28318530717958647692f
+#define ORC_R2 0.70710678118654752440f
+#define ORC_C16 0.92387953251128673848f
+#define ORC_S16 0.38268343236508977173f
+
+static inline cpx mk(float re, float im) { cpx r; r.re = re; r.im = im; return r; }
+static inline cpx cadd(cpx a, cpx b) { return mk(a.re + b.re, a.im + b.im); }
+static inline cpx csub(cpx a, cpx b) { return mk(a.re - b.re, a.im - b.im); }
+
+/* complex multiply with two fused products: verify_kernel.cpp:33-37 */
+static inline cpx cmul(cpx a, cpx b)
+{
+   return mk(fmaf(a.re, b.re, -a.im * b.im), fmaf(a.re, b.im, a.im * b.re));
+}
+
+/* conjugate multiply a * conj(b): fufft.cuh:644-648 (MidConjMultiply) */
+static inline cpx cmul_conj(cpx x, cpx y)
+{
+   return mk(fmaf(x.re, y.re, x.im * y.im), fmaf(x.im, y.re, -x.re * y.im));
+}
+
+/* x * (+-i), x * w^1, x * w^3 in the specialised (CPP_OPT) forms:
+ * verify_kernel.cpp:39-60 */
+static inline cpx mul_i(cpx a, int s) { return s < 0 ? mk(a.im, -a.re) : mk(-a.im, a.re); }
+static inline cpx mul_w1(cpx a, int s)
+{
+   const float x = a.re, y = a.im;
+   return s < 0 ? mk(ORC_R2 * (x + y), ORC_R2 * (y - x)) : mk(ORC_R2 * (x - y), ORC_R2 * (x + y));
+}
+static inline cpx mul_w3(cpx a, int s)
+{
+   const float x = a.re, y = a.im;
+   return s < 0 ? mk(ORC_R2 * (y - x), ORC_R2 * (-x - y)) : mk(ORC_R2 * (-x - y), ORC_R2 * (x - y));
+}
+
+/* radix-8 as three radix-2 stages, natural-order output: verify_kernel.cpp:62-86 */
+static void dft8(const cpx u[8], cpx v[8], int s)
+{
+   cpx a0 = cadd(u[0], u[4]), a1 = cadd(u[1], u[5]), a2 = cadd(u[2], u[6]), a3 = cadd(u[3], u[7]);
+   cpx a4 = csub(u[0], u[4]);
+   cpx a5 = mul_w1(csub(u[1], u[5]), s);
+   cpx a6 = mul_i(csub(u[2], u[6]), s);
+   cpx a7 = mul_w3(csub(u[3], u[7]), s);
+   cpx b0 = cadd(a0, a2), b1 = cadd(a1, a3), b2 = csub(a0, a2);
+   cpx b3 = mul_i(csub(a1, a3), s);
+   cpx b4 = cadd(a4, a6), b5 = cadd(a5, a7), b6 = csub(a4, a6);
+   cpx b7 = mul_i(csub(a5, a7), s);
+   v[0] = cadd(b0, b1); v[4] = csub(b0, b1);
+   v[2] = cadd(b2, b3); v[6] = csub(b2, b3);
+   v[1] = cadd(b4, b5); v[5] = csub(b4, b5);
+   v[3] = cadd(b6, b7); v[7] = csub(b6, b7);
+}
+
+/* radix-2 / radix-4: verify_kernel.cpp:158-171 */
+static void dft2(const cpx u[2], cpx v[2]) { v[0] = cadd(u[0], u[1]); v[1] = csub(u[0], u[1]); }
+static void dft4(const cpx u[4], cpx v[4], int s)
+{
+   cpx a0 = cadd(u[0], u[2]), a1 = cadd(u[1], u[3]);
+   cpx a2 = csub(u[0], u[2]);
+   cpx a3 = mul_i(csub(u[1], u[3]), s);
+   v[0] = cadd(a0, a1); v[2] = csub(a0, a1);
+   v[1] = cadd(a2, a3); v[3] = csub(a2, a3);
+}
+
+/* x * W16^k with the cheap forms for k = 2, 4, 6: verify_kernel.cpp:842-855 */
+static cpx mul_w16(int k, cpx x, int s)
+{
+   const float sf = (float)s;
+   switch(k) {
+   case 0: return x;
+   case 1: return cmul(x, mk(ORC_C16, sf * ORC_S16));
+   case 2: return mul_w1(x, s);
+   case 3: return cmul(x, mk(ORC_S16, sf * ORC_C16));
+   case 4: return mul_i(x, s);
+   case 5: return cmul(x, mk(-ORC_S16, sf * ORC_C16));
+   case 6: return mul_w3(x, s);
+   default: return cmul(x, mk(-ORC_C16, sf * ORC_S16));
+   }
+}
+
+/* radix-16 = one radix-2 stage feeding two radix-8s, outputs interleaved:
+ * verify_kernel.cpp:962-972 */
+static void dft16(const cpx u[16], cpx v[16], int s)
+{
+   cpx a[8], b[8], va[8], vb[8];
+   for(int k = 0; k < 8; k++) {
+      a[k] = cadd(u[k], u[k + 8]);
+      b[k] = mul_w16(k, csub(u[k], u[k + 8]), s);
+   }
+   dft8(a, va, s);
+   dft8(b, vb, s);
+   for(int k = 0; k < 8; k++) { v[2 * k] = va[k]; v[2 * k + 1] = vb[k]; }
+}
+
+static void dftR(int R, const cpx* u, cpx* v, int s)
+{
+   if(R == 2) dft2(u, v);
+   else if(R == 4) dft4(u, v, s);
+   else if(R == 8) dft8(u, v, s);
+   else dft16(u, v, s);
+}
+
+/* cosf/sinf twiddle: verify_kernel.cpp:31 */
+static inline cpx twiddle(float ang) { return mk(cosf(ang), sinf(ang)); }
+
+/* one sincos for W^j, the rest W^(jk) by the running product w <- w * W^j:
+ * verify_kernel.cpp:180-191 */
+static void tw_chain(int R, cpx* x, float step, int j)
+{
+   const cpx w1 = twiddle(step * (float)j);
+   cpx w = w1;
+   x[1] = cmul(x[1], w);
+   for(int k = 2; k < R; k++) { w = cmul(w, w1); x[k] = cmul(x[k], w); }
+}
+
+/* radix-16 twiddles as two chains of W^2 (even / odd outputs):
+ * verify_kernel.cpp:974-986 */
+static void tw_split16(cpx x[16], float step, int j)
+{
+   const cpx w1 = twiddle(step * (float)j);
+   const cpx w2 = cmul(w1, w1);
+   x[1] = cmul(x[1], w1);
+   cpx ze = w2, zo = cmul(w2, w1);
+   for(int m = 1; m < 8; m++) {
+      x[2 * m] = cmul(x[2 * m], ze);
+      x[2 * m + 1] = cmul(x[2 * m + 1], zo);
+      if(m < 7) { ze = cmul(ze, w2); zo = cmul(zo, w2); }
+   }
+}
+
+/*
+ * One in-place radix-R pass at stride M over an array holding whole butterfly
+ * groups.  Group g owns taps base + k*M, base = (g/M)*R*M + g%M.  DIF: butterfly
+ * then twiddle W_{RM}^{jk}; DIT: twiddle then butterfly; no twiddle at M == 1.
+ *   in-block passes (V=8): verify_kernel.cpp:194-209
+ *   in-block passes (V=16, split16 = 1): verify_kernel.cpp:988-1010
+ *   flat outer passes over the whole batch: verify_kernel.cpp:319-337
+ * split16 selects the even/odd twiddle chains for R == 16 (in-block V=16
+ * passes); the flat outer passes use the single running chain for every R.
+ */
+static void pass_inplace(cpx* A, size_t ngroups, int R, int M, int sign, int dit, int split16)
+{
+   const float step = (float)sign * ORC_2PI_F / (float)(R * M);
+   for(size_t g = 0; g < ngroups; g++) {
+      const size_t j = g % (size_t)M, b = g / (size_t)M;
+      const size_t base = b * (size_t)R * (size_t)M + j;
+      cpx u[16], v[16];
+      for(int k = 0; k < R; k++) u[k] = A[base + (size_t)k * M];
+      if(dit && M > 1) {
+         if(R == 16 && split16) tw_split16(u, step, (int)j); else tw_chain(R, u, step, (int)j);
+      }
+      dftR(R, u, v, sign);
+      if(!dit && M > 1) {
+         if(R == 16 && split16) tw_split16(v, step, (int)j); else tw_chain(R, v, step, (int)j);
+      }
+      for(int k = 0; k < R; k++) A[base + (size_t)k * M] = v[k];
+   }
+}
+
+/* ---- factorisation and index maps ---------------------------------------- */
+
+static int ilog2i(long long n) { int m = 0; while((1LL << m) < n) m++; return m; }
+
+/* N = lead * R^nr with the leftover bits in one leading pass:
+ * verify_kernel.cpp:126-139 (radix 8 / 16), cpu_mixed.cpp:36-49 */
+int orc_factorise(int n, int radix, int* lead, int* nr)
+{
+   const int m = ilog2i(n), rb = ilog2i(radix);
+   if((1 << m) != n || (1 << rb) != radix) return -1;
+   *nr = m / rb;
+   *lead = 1 << (m % rb);
+   return 0;
+}
+
+/* Digit order a DIF chain leaves its spectrum in: bit groups of the radix
+ * widths in pass order, read MSB-first, written back in reverse order.
+ * verify_kernel.cpp:460-477 (chain_rev); mixedrev :145-156 and mixedrev16
+ * :946-956 are the cases [lead, 8, 8, ...] and [lead, 16, 16, ...]. */
+long long orc_chain_rev(long long idx, const int* radices, int nrad)
+{
+   int w[64], m = 0;
+   for(int k = 0; k < nrad; k++) { w[k] = ilog2i(radices[k]); m += w[k]; }
+   long long d[64];
+   int pos = m;
+   for(int k = 0; k < nrad; k++) { pos -= w[k]; d[k] = (idx >> pos) & ((1LL << w[k]) - 1); }
+   long long out = 0;
+   int op = m;
+   for(int k = nrad - 1; k >= 0; k--) { op -= w[k]; out |= d[k] << op; }
+   return out;
+}
+
+/* radix chain of a one-block transform: [lead (if > 1), R, R, ...] */
+static int chain_of(int n, int radix, int* rad)
+{
+   int lead, nr, p = 0;
+   if(orc_factorise(n, radix, &lead, &nr)) return -1;
+   if(lead > 1) rad[p++] = lead;
+   for(int i = 0; i < nr; i++) rad[p++] = radix;
+   return p;
+}
+
+/* b_dr[t*N + i] = b[t*N + rev(i)] for the one-block radix chain:
+ * verify_kernel.cpp:1298-1301 (radix 8), :1355-1358 (radix 16) */
+int orc_permute_dr(const cpx* b, cpx* out, int n, int batch, int radix)
+{
+   int rad[32];
+   const int nrad = chain_of(n, radix, rad);
+   if(nrad < 0) return -1;
+   for(int i = 0; i < n; i++) {
+      const long long r = orc_chain_rev(i, rad, nrad);
+      for(int t = 0; t < batch; t++) out[(size_t)t * n + i] = b[(size_t)t * n + r];
+   }
+   return 0;
+}
+
+/* register-boundary layout: bperm[L + k*T] = b_dr[V*L + k], T = N/V:
+ * verify_kernel.cpp:1339-1344 (V=8), :1382-1387 (V=16) */
+int orc_bperm(const cpx* b_dr, cpx* out, int n, int batch, int v)
+{
+   if(n % v) return -1;
+   const int T = n / v;
+   for(int t = 0; t < batch; t++)
+      for(int L = 0; L < T; L++)
+         for(int k = 0; k < v; k++)
+            out[(size_t)t * n + L + (size_t)k * T] = b_dr[(size_t)t * n + (size_t)v * L + k];
+   return 0;
+}
+
+/* ---- one-block fused pipelines ------------------------------------------- */
+
+enum { ORC_MID_NONE = 0, ORC_MID_MULTIPLY = 1, ORC_MID_CONJ = 2 };
+
+static void dif_chain(cpx* A, size_t count, int n, int radix)
+{
+   int lead, nr;
+   orc_factorise(n, radix, &lead, &nr);
+   const int split16 = (radix == 16);
+   const size_t tr = count / (size_t)n;
+   int M = n / lead;
+   if(lead > 1) pass_inplace(A, tr * (size_t)(n / lead), lead, M, -1, 0, split16);
+   for(int s = 0; s < nr; s++) { M /= radix; pass_inplace(A, tr * (size_t)(n / radix), radix, M, -1, 0, split16); }
+}
+
+static void dit_chain(cpx* A, size_t count, int n, int radix)
+{
+   int lead, nr;
+   orc_factorise(n, radix, &lead, &nr);
+   const int split16 = (radix == 16);
+   const size_t tr = count / (size_t)n;
+   int M = 1;
+   for(int s = 0; s < nr; s++) { pass_inplace(A, tr * (size_t)(n / radix), radix, M, +1, 1, split16); M *= radix; }
+   if(lead > 1) pass_inplace(A, tr * (size_t)(n / lead), lead, M, +1, 1, split16);
+}
+
+static void apply_mid(cpx* A, const cpx* b, size_t count, int mid, int n, long long filter_stride)
+{
+   /* filter_stride: elements between consecutive transforms' filters (n for
+    * one filter per transform, 0 for one filter broadcast over the batch) */
+   for(size_t i = 0; i < count; i++) {
+      const size_t t = i / (size_t)n, p = i % (size_t)n;
+      const cpx y = b[(size_t)((long long)t * filter_stride) + p];
+      if(mid == ORC_MID_MULTIPLY) A[i] = cmul(A[i], y);
+      else if(mid == ORC_MID_CONJ) A[i] = cmul_conj(A[i], y);
+   }
+}
+
+/*
+ * Fused cyclic convolution of one-block transforms: natural-order input, DIF
+ * chain (lead pass then radix passes), pointwise mid-op against the filter in
+ * chain-reversed order, DIT chain back to natural order.
+ *   radix 8:  kernel_pipeline_ip, verify_kernel.cpp:211-244 (fufft.cuh:930-967)
+ *   radix 16: kernel_pipeline_v16, verify_kernel.cpp:1051-1082 (fufft.cuh:763-800)
+ * The register-boundary variants (kernel_pipeline_fused :247-286,
+ * kernel_pipeline_v16f :1012-1049) run the same operations in the same order
+ * and are therefore this function with the filter read through orc_bperm.
+ */
+int orc_conv(int n, int radix, int mid, const cpx* a, const cpx* b_dr, cpx* out, int batch,
+             long long filter_stride)
+{
+   int lead, nr;
+   if(orc_factorise(n, radix, &lead, &nr)) return -1;
+   const size_t count = (size_t)n * batch;
+   if(out != a) memcpy(out, a, count * sizeof(cpx));
+   dif_chain(out, count, n, radix);
+   apply_mid(out, b_dr, count, mid, n, filter_stride);
+   dit_chain(out, count, n, radix);
+   return 0;
+}
+
+/* split forward: natural in, chain-reversed spectrum out.
+ * kernel_pipeline_fwd, verify_kernel.cpp:794-813 (fufft.cuh:1343-1373) */
+int orc_fwd(int n, int radix, const cpx* a, cpx* spec, int batch)
+{
+   int lead, nr;
+   if(orc_factorise(n, radix, &lead, &nr)) return -1;
+   const size_t count = (size_t)n * batch;
+   if(spec != a) memcpy(spec, a, count * sizeof(cpx));
+   dif_chain(spec, count, n, radix);
+   return 0;
+}
+
+/* split apply: spectrum (x) filter, then DIT.  kernel_pipeline_apply,
+ * verify_kernel.cpp:815-836 (fufft.cuh:1375-1407; multiply only there, the
+ * conjugate form is this library's addition) */
+int orc_apply(int n, int radix, int mid, const cpx* spec, const cpx* b_dr, cpx* out, int batch,
+              long long filter_stride)
+{
+   int lead, nr;
+   if(orc_factorise(n, radix, &lead, &nr)) return -1;
+   const size_t count = (size_t)n * batch;
+   if(out != spec) memcpy(out, spec, count * sizeof(cpx));
+   apply_mid(out, b_dr, count, mid, n, filter_stride);
+   dit_chain(out, count, n, radix);
+   return 0;
+}
+
+/* two-for-one real convolution: pack (xr, yr) as re/im, conv with the
+ * spectrum of a REAL filter, unpack.  kernel_conv_r2, verify_kernel.cpp:580-615
+ * (fufft.cuh:1273-1330) */
+int orc_conv_r2(int n, int radix, const float* xr, const float* yr, const cpx* b_dr,
+                float* ur, float* vr, int batch, long long filter_stride)
+{
+   const size_t count = (size_t)n * batch;
+   cpx* A = (cpx*)malloc(count * sizeof(cpx));
+   if(!A) return -2;
+   for(size_t i = 0; i < count; i++) A[i] = mk(xr[i], yr[i]);
+   int rc = orc_conv(n, radix, ORC_MID_MULTIPLY, A, b_dr, A, batch, filter_stride);
+   for(size_t i = 0; i < count; i++) { ur[i] = A[i].re; vr[i] = A[i].im; }
+   free(A);
+   return rc;
+}
+
+/* ---- 2-D ----------------------------------------------------------------- */
+
+/* column pass of the fused 2-D conv: taps at stride W*m, twiddle period 8m
+ * indexed by the row position inside the column group.
+ * dev_col_pass, verify_kernel.cpp:681-698 (fufft.cuh:1185-1207) */
+static void col_pass(cpx* A, int H, int W, int m, int sign, int dit)
+{
+   const float step = (float)sign * ORC_2PI_F / (float)(8 * m);
+   const int T = H * W / 8;
+   for(int lane = 0; lane < T; lane++) {
+      const int c = lane % W, g2 = lane / W, j2 = g2 % m, b2 = g2 / m;
+      const int base = c + W * (b2 * 8 * m + j2);
+      cpx u[8], v[8];
+      for(int k = 0; k < 8; k++) u[k] = A[base + k * W * m];
+      if(dit && m > 1) tw_chain(8, u, step, j2);
+      dft8(u, v, sign);
+      if(!dit && m > 1) tw_chain(8, v, step, j2);
+      for(int k = 0; k < 8; k++) A[base + k * W * m] = v[k];
+   }
+}
+
+/* fused 2-D conv for H, W powers of 8 (H*W <= 4096 in the reference):
+ * rows DIF, columns DIF, pointwise, columns DIT, rows DIT.  Filter slot (r, c)
+ * holds spectrum (rev8_H(r), rev8_W(c)).  kernel_conv2d,
+ * verify_kernel.cpp:700-722 (fufft.cuh:1209-1258) */
+int orc_conv2d_pow8(int H, int W, const cpx* a, const cpx* b2d, cpx* out, int batch,
+                    long long filter_stride)
+{
+   int lh, nh, lw, nw;
+   if(orc_factorise(H, 8, &lh, &nh) || orc_factorise(W, 8, &lw, &nw) || lh != 1 || lw != 1) return -1;
+   const int NP = H * W;
+   for(int t = 0; t < batch; t++) {
+      cpx* A = out + (size_t)t * NP;
+      const cpx* b = b2d + (size_t)((long long)t * filter_stride);
+      if(out != a) memcpy(A, a + (size_t)t * NP, (size_t)NP * sizeof(cpx));
+      for(int M = W / 8; M >= 1; M /= 8) pass_inplace(A, NP / 8, 8, M, -1, 0, 0);
+      for(int m = H / 8; m >= 1; m /= 8) col_pass(A, H, W, m, -1, 0);
+      for(int i = 0; i < NP; i++) A[i] = cmul(A[i], b[i]);
+      for(int m = 1; m <= H / 8; m *= 8) col_pass(A, H, W, m, +1, 1);
+      for(int M = 1; M <= W / 8; M *= 8) pass_inplace(A, NP / 8, 8, M, +1, 1, 0);
+   }
+   return 0;
+}
+
+/* ---- int16 block floating point ------------------------------------------ */
+
+/* one fp32 scale per transform: mx = max|re|,|im| (>= 1e-30), inv = 32767/mx,
+ * q = rint(clamp(x*inv, +-32767)), scale = mx/32767.
+ * bfp_quantize, verify_kernel.cpp:1092-1105; bfp_quant_host,
+ * bench_fufft.cu:107-117 (same result: the 1e-30 floor commutes with max). */
+void orc_bfp_quantize(const cpx* x, int n, int16_t* q /* interleaved re,im */, float* scale)
+{
+   float mx = 0.0f;
+   for(int i = 0; i < n; i++) {
+      const float ax = fabsf(x[i].re), ay = fabsf(x[i].im);
+      const float m2 = ax > ay ? ax : ay;
+      if(m2 > mx) mx = m2;
+   }
+   if(mx < 1e-30f) mx = 1e-30f;
+   const float inv = 32767.0f / mx;
+   *scale = mx / 32767.0f;
+   for(int i = 0; i < n; i++) {
+      float vx = x[i].re * inv, vy = x[i].im * inv;
+      vx = vx < -32767.0f ? -32767.0f : (vx > 32767.0f ? 32767.0f : vx);
+      vy = vy < -32767.0f ? -32767.0f : (vy > 32767.0f ? 32767.0f : vy);
+      q[2 * i] = (int16_t)lrintf(vx);
+      q[2 * i + 1] = (int16_t)lrintf(vy);
+   }
+}
+
+void orc_bfp_quantize_batch(const cpx* x, int n, int batch, int16_t* q, float* scale)
+{
+   for(int t = 0; t < batch; t++)
+      orc_bfp_quantize(x + (size_t)t * n, n, q + (size_t)2 * t * n, scale + t);
+}
+
+void orc_bfp_dequantize_batch(const int16_t* q, const float* scale, int n, int batch, cpx* x)
+{
+   for(int t = 0; t < batch; t++)
+      for(int i = 0; i < n; i++) {
+         const size_t k = (size_t)t * n + i;
+         x[k] = mk((float)q[2 * k] * scale[t], (float)q[2 * k + 1] * scale[t]);
+      }
+}
+
+/* BFP fused conv: dequantise, radix-16 DIF, multiply by the dequantised
+ * filter (chain-reversed, linear layout), DIT, per-transform abs-max and
+ * requantise.  kernel_v16_bfp, verify_kernel.cpp:1109-1135
+ * (fufft.cuh:1614-1701).  radix 8 runs the same steps on the radix-8 chain. */
+int orc_conv_bfp(int n, int radix, int mid, const int16_t* aq, const float* as, const int16_t* bq,
+                 const float* bs, int16_t* oq, float* os, int batch, long long filter_stride)
+{
+   int lead, nr;
+   if(orc_factorise(n, radix, &lead, &nr)) return -1;
+   cpx* A = (cpx*)malloc((size_t)n * sizeof(cpx));
+   cpx* B = (cpx*)malloc((size_t)n * sizeof(cpx));
+   if(!A || !B) { free(A); free(B); return -2; }
+   for(int t = 0; t < batch; t++) {
+      const size_t off = (size_t)t * n;
+      const size_t foff = (size_t)((long long)t * filter_stride);
+      const size_t fsc = filter_stride ? (size_t)t : 0;
+      for(int i = 0; i < n; i++) A[i] = mk((float)aq[2 * (off + i)] * as[t], (float)aq[2 * (off + i) + 1] * as[t]);
+      for(int i = 0; i < n; i++) B[i] = mk((float)bq[2 * (foff + i)] * bs[fsc], (float)bq[2 * (foff + i) + 1] * bs[fsc]);
+      dif_chain(A, (size_t)n, n, radix);
+      apply_mid(A, B, (size_t)n, mid, n, 0);
+      dit_chain(A, (size_t)n, n, radix);
+      orc_bfp_quantize(A, n, oq + 2 * off, os + t);
+   }
+   free(A); free(B);
+   return 0;
+}
+
+/* ---- four-step large N ----------------------------------------------------- */
+
+/* Middle of size MID under base radix R: lead pass first when MID is not a
+ * pure power of R.  mid_radices, verify_kernel.cpp:302-310 */
+static int mid_radices(int mid, int R, int* out)
+{
+   int k = 0, m = mid, p = 0;
+   while(m % R == 0) { m /= R; k++; }
+   if(m > 1) out[p++] = m;
+   for(int i = 0; i < k; i++) out[p++] = R;
+   return p;
+}
+
+/* radix chain of the four-step: [R_OUT] x LOUT ++ middle chain (radix 8 or 16).
+ * test_large_cfg, verify_kernel.cpp:481-485 */
+int orc_foursteps_chain(long long n, int r_out, int mid, int mid_radix, int* rad)
+{
+   int p = 0;
+   for(long long M = n / r_out; M >= mid; M /= r_out) rad[p++] = r_out;
+   p += mid_radices(mid, mid_radix, rad + p);
+   return p;
+}
+
+/* outer flat passes around a one-block middle (radix-16 V=16 or radix-8) on
+ * chunks of MID.  conv_foursteps_cfg, verify_kernel.cpp:373-394
+ * (bench_fufft.cu:443-451) */
+int orc_conv_foursteps(long long n, int batch, int r_out, int mid, int mid_radix, cpx* A, const cpx* b_dr)
+{
+   const size_t count = (size_t)n * batch;
+   const size_t ng = (size_t)batch * (size_t)(n / r_out);
+   for(long long M = n / r_out; M >= mid; M /= r_out) pass_inplace(A, ng, r_out, (int)M, -1, 0, 0);
+   orc_conv(mid, mid_radix, ORC_MID_MULTIPLY, A, b_dr, A, (int)(count / (size_t)mid), mid);
+   for(long long M = mid; M <= n / r_out; M *= r_out) pass_inplace(A, ng, r_out, (int)M, +1, 1, 0);
+   return 0;
+}
+
+/* the same radix sequence applied as flat passes over the whole transform.
+ * conv_monolithic_cfg, verify_kernel.cpp:397-419 */
+int orc_conv_monolithic(long long n, int batch, int r_out, int mid, int mid_radix, cpx* A, const cpx* b_dr)
+{
+   int rad[64];
+   const int p = orc_foursteps_chain(n, r_out, mid, mid_radix, rad);
+   long long M = n;
+   for(int k = 0; k < p; k++) {
+      M /= rad[k];
+      pass_inplace(A, (size_t)batch * (size_t)(n / rad[k]), rad[k], (int)M, -1, 0, 0);
+   }
+   const size_t count = (size_t)n * batch;
+   for(size_t i = 0; i < count; i++) A[i] = cmul(A[i], b_dr[i]);
+   for(int k = p - 1; k >= 0; k--) {
+      pass_inplace(A, (size_t)batch * (size_t)(n / rad[k]), rad[k], (int)M, +1, 1, 0);
+      M *= rad[k];
+   }
+   return 0;
+}
+
+/* ---- fp64 ground truth ----------------------------------------------------- */
+
+/* iterative radix-2 Cooley-Tukey in fp64: verify_kernel.cpp:434-456 */
+void orc_fft2_f64(cpxd* x, int n, int sign)
+{
+   for(int i = 1, j = 0; i < n; i++) {
+      int bit = n >> 1;
+      for(; j & bit; bit >>= 1) j ^= bit;
+      j ^= bit;
+      if(i < j) { cpxd t = x[i]; x[i] = x[j]; x[j] = t; }
+   }
+   const double PI = 3.14159265358979323846;
+   for(int len = 2; len <= n; len <<= 1) {
+      const double ang = sign * 2.0 * PI / (double)len;
+      const double wr = cos(ang), wi = sin(ang);
+      for(int i = 0; i < n; i += len) {
+         double cr = 1.0, ci = 0.0;
+         for(int k = 0; k < len / 2; k++) {
+            cpxd a0 = x[i + k], a1 = x[i + k + len / 2];
+            const double tr = a1.re * cr - a1.im * ci, ti = a1.re * ci + a1.im * cr;
+            x[i + k].re = a0.re + tr; x[i + k].im = a0.im + ti;
+            x[i + k + len / 2].re = a0.re - tr; x[i + k + len / 2].im = a0.im - ti;
+            const double nr = cr * wr - ci * wi, ni = cr * wi + ci * wr;
+            cr = nr; ci = ni;
+         }
+      }
+   }
+}
+
+/* fp64 cyclic convolution of natural-order signal and natural-order spectrum:
+ * IDFT(DFT(a) . b), the quantity every fused kernel computes (with 1/N folded
+ * into b).  verify_kernel.cpp:1305-1321 / :506-516 */
+void orc_conv_f64(const cpx* a, const cpx* bnat, double* out /* interleaved */, int n, int batch,
+                  long long filter_stride)
+{
+   cpxd* x = (cpxd*)malloc((size_t)n * sizeof(cpxd));
+   for(int t = 0; t < batch; t++) {
+      const cpx* at = a + (size_t)t * n;
+      const cpx* bt = bnat + (size_t)((long long)t * filter_stride);
+      for(int i = 0; i < n; i++) { x[i].re = at[i].re; x[i].im = at[i].im; }
+      orc_fft2_f64(x, n, -1);
+      for(int i = 0; i < n; i++) {
+         const double br = bt[i].re, bi = bt[i].im;
+         const double r = x[i].re * br - x[i].im * bi, im = x[i].re * bi + x[i].im * br;
+         x[i].re = r; x[i].im = im;
+      }
+      orc_fft2_f64(x, n, +1);
+      for(int i = 0; i < n; i++) { out[2 * ((size_t)t * n + i)] = x[i].re; out[2 * ((size_t)t * n + i) + 1] = x[i].im; }
+   }
+   free(x);
+}
+
+/* fp64 2-D cyclic convolution via row and column radix-2 FFTs:
+ * test_2d, verify_kernel.cpp:753-777 */
+void orc_conv2d_f64(const cpx* a, const cpx* bnat, double* out, int H, int W, int batch,
+                    long long filter_stride)
+{
+   const int NP = H * W;
+   cpxd* X = (cpxd*)malloc((size_t)NP * sizeof(cpxd));
+   cpxd* line = (cpxd*)malloc((size_t)(H > W ? H : W) * sizeof(cpxd));
+   for(int t = 0; t < batch; t++) {
+      const cpx* at = a + (size_t)t * NP;
+      const cpx* bt = bnat + (size_t)((long long)t * filter_stride);
+      for(int i = 0; i < NP; i++) { X[i].re = at[i].re; X[i].im = at[i].im; }
+      for(int pass = 0; pass < 2; pass++) {
+         const int sign = pass == 0 ? -1 : +1;
+         if(pass == 1) {
+            for(int i = 0; i < NP; i++) {
+               const double br = bt[i].re, bi = bt[i].im;
+               const double r = X[i].re * br - X[i].im * bi, im = X[i].re * bi + X[i].im * br;
+               X[i].re = r; X[i].im = im;
+            }
+         }
+         for(int r = 0; r < H; r++) {
+            for(int c = 0; c < W; c++) line[c] = X[r * W + c];
+            orc_fft2_f64(line, W, sign);
+            for(int c = 0; c < W; c++) X[r * W + c] = line[c];
+         }
+         for(int c = 0; c < W; c++) {
+            for(int r = 0; r < H; r++) line[r] = X[r * W + c];
+            orc_fft2_f64(line, H, sign);
+            for(int r = 0; r < H; r++) X[r * W + c] = line[r];
+         }
+      }
+      for(int i = 0; i < NP; i++) { out[2 * ((size_t)t * NP + i)] = X[i].re; out[2 * ((size_t)t * NP + i) + 1] = X[i].im; }
+   }
+   free(X); free(line);
+}
+
+/* naive fp64 DFT: verify_kernel.cpp:1235-1247 */
+void orc_ref_dft(const cpxd* in, cpxd* out, int n, int sign)
+{
+   const double PI = 3.14159265358979323846;
+   for(int k = 0; k < n; k++) {
+      double ar = 0, ai = 0;
+      for(int j = 0; j < n; j++) {
+         const double t = sign * 2.0 * PI * (double)k * (double)j / (double)n;
+         const double c = cos(t), s = sin(t);
+         ar += in[j].re * c - in[j].im * s;
+         ai += in[j].re * s + in[j].im * c;
+      }
+      out[k].re = ar; out[k].im = ai;
+   }
+}
+
+/* ---- seeded inputs of the reference's tests ------------------------------ */
+
+/* MT19937 (Matsumoto & Nishimura 1998) with the std::mt19937 seeding rule,
+ * feeding std::uniform_real_distribution<float>(-1, 1) as libstdc++ computes
+ * it: generate_canonical<float, 24> takes one 32-bit draw x and returns
+ * (float)x / 2^32 (clamped below 1), then the distribution returns u*2 + (-1).
+ * The reference's tests draw their inputs this way (verify_kernel.cpp:1277-1286
+ * and the other test_* functions); the stream is pinned against the compiled
+ * reference by tests/test_oracle_golden.py. */
+void orc_uniform_stream(uint32_t seed, long long count, float* out)
+{
+   uint32_t mt[624];
+   int idx = 624;
+   mt[0] = seed;
+   for(int i = 1; i < 624; i++) mt[i] = 1812433253u * (mt[i - 1] ^ (mt[i - 1] >> 30)) + (uint32_t)i;
+   for(long long c = 0; c < count; c++) {
+      if(idx >= 624) {
+         for(int i = 0; i < 624; i++) {
+            const uint32_t y = (mt[i] & 0x80000000u) | (mt[(i + 1) % 624] & 0x7fffffffu);
+            mt[i] = mt[(i + 397) % 624] ^ (y >> 1) ^ ((y & 1u) ? 0x9908b0dfu : 0u);
+         }
+         idx = 0;
+      }
+      uint32_t y = mt[idx++];
+      y ^= y >> 11;
+      y ^= (y << 7) & 0x9d2c5680u;
+      y ^= (y << 15) & 0xefc60000u;
+      y ^= y >> 18;
+      float u = (float)y / 4294967296.0f;
+      if(u >= 1.0f) u = nextafterf(1.0f, 0.0f);
+      out[c] = u * 2.0f + -1.0f;
+   }
+}

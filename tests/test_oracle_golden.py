@@ -1,0 +1,124 @@
+"""Pins the oracle (oracle/fufft_oracle.c) to the reference's own transcription.
+
+Every case below is one of the reference's seeded tests (verify_kernel.cpp).
+The fixtures in tests/golden/ were produced by the reference code itself
+(tests/golden/make_golden.py over oracle/_ref); here the oracle regenerates
+each input from the same seed and recomputes each output, and both must
+match the recorded SHA-256 digests bit for bit.
+"""
+import hashlib
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle.oracle import MID_MULTIPLY, rel_l2
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+with open(os.path.join(GOLD, "reference_digests.json")) as f:
+    DIG = json.load(f)
+
+
+def _d(x):
+    return hashlib.sha256(np.ascontiguousarray(x).tobytes()).hexdigest()
+
+
+def _cases(prefix):
+    return [k for k in DIG if k.startswith(prefix + "/")]
+
+
+def test_reference_suite_passed_when_fixtures_were_made():
+    assert DIG["suite_all_pass"] is True
+
+
+@pytest.mark.parametrize("key", _cases("conv"))
+def test_conv_family_bit_exact(oracle, key):
+    _, n, cpb, batch = key.split("/")
+    n, cpb, batch = int(n), int(cpb), int(batch)
+    rec = DIG[key]
+    a, b = oracle.gen_test(n, cpb, batch)
+    assert _d(a) == rec["a"] and _d(b) == rec["b"], "seeded generator drifted"
+    b8 = oracle.permute_dr(b, n, 8)
+    ip = oracle.conv(a, b8, n, 8)
+    assert _d(ip) == rec["ip"]
+    assert _d(ip) == rec["fused"]          # register boundary == in-place, bit for bit
+    spec = oracle.fwd(a, n, 8)
+    assert _d(spec) == rec["fwd"]
+    assert _d(oracle.apply(spec, b8, n, 8)) == rec["apply"]
+    assert rec["apply"] == rec["ip"]       # split fwd/apply == fused
+    if "v16" in rec:
+        v16 = oracle.conv(a, oracle.permute_dr(b, n, 16), n, 16)
+        assert _d(v16) == rec["v16"] == rec["v16f"]
+    ref64 = oracle.conv_f64(a, b, n)
+    assert rel_l2(ip, ref64) < 3e-6       # verify_kernel.cpp:1395
+
+
+@pytest.mark.parametrize("key", _cases("bfp"))
+def test_bfp_bit_exact(oracle, key):
+    _, n, seed = key.split("/")
+    n, seed = int(n), int(seed)
+    rec = DIG[key]
+    a, b = oracle.gen_bfp(n, seed)
+    assert _d(a) == rec["a"] and _d(b) == rec["b"]
+    aq, as_ = oracle.bfp_quantize(a, n)
+    bq, bs = oracle.bfp_quantize(oracle.permute_dr(b, n, 16), n)
+    assert _d(aq) == rec["aq"] and _d(as_) == rec["a_scale"]
+    assert _d(bq) == rec["bq"] and _d(bs) == rec["b_scale"]
+    oq, os_ = oracle.conv_bfp(aq, as_, bq, bs, n, 16)
+    assert _d(oq) == rec["oq"] and _d(os_) == rec["o_scale"]
+    got = oracle.bfp_dequantize(oq, os_, n)
+    rel = rel_l2(got, oracle.conv_f64(a, b, n))
+    assert rel < 3e-4 and -np.log2(rel) >= 12.0      # verify_kernel.cpp:1176
+
+
+@pytest.mark.parametrize("key", _cases("r2"))
+def test_r2_bit_exact(oracle, key):
+    _, n, cpb, batch = key.split("/")
+    n, batch = int(n), int(batch)
+    rec = DIG[key]
+    xr, yr, h = oracle.gen_r2_signals(n, batch)
+    assert _d(xr) == rec["xr"] and _d(yr) == rec["yr"] and _d(h) == rec["h"]
+    g = np.load(os.path.join(GOLD, "reference_cases.npz"))
+    b_dr = g[key + "/b_dr"]                 # fp64 spectrum rounded by the reference
+    assert _d(b_dr) == rec["b_dr"]
+    ur, vr = oracle.conv_r2(xr, yr, b_dr, n, 8)
+    assert _d(ur) == rec["ur"] and _d(vr) == rec["vr"]
+
+
+@pytest.mark.parametrize("key", _cases("conv2d"))
+def test_conv2d_bit_exact(oracle, key):
+    _, h, w, batch = key.split("/")
+    h, w, batch = int(h), int(w), int(batch)
+    rec = DIG[key]
+    a, b = oracle.gen_2d(h, w, batch)
+    assert _d(a) == rec["a"] and _d(b) == rec["b"]
+    rows = oracle.rev_table(oracle.chain(h, 8), h)
+    cols = oracle.rev_table(oracle.chain(w, 8), w)
+    b2 = np.ascontiguousarray(b.reshape(batch, h, w)[:, rows][:, :, cols]).ravel()
+    assert _d(b2) == rec["b_dr"]
+    out = oracle.conv2d_pow8(a, b2, h, w)
+    assert _d(out) == rec["out"]
+    assert rel_l2(out, oracle.conv2d_f64(a, b, h, w)) < 3e-6     # verify_kernel.cpp:786
+
+
+@pytest.mark.parametrize("key", _cases("large"))
+def test_foursteps_bit_exact(oracle, key):
+    _, n, batch, r_out, mid, v16 = key.split("/")
+    n, batch, r_out, mid, v16 = int(n), int(batch), int(r_out), int(mid), int(v16)
+    rec = DIG[key]
+    a, b = oracle.gen_large_cfg(n, batch, r_out, mid)
+    assert _d(a) == rec["a"] and _d(b) == rec["b"]
+    chain = oracle.foursteps_chain(n, r_out, mid, 16 if v16 else 8)
+    b_dr = np.ascontiguousarray(b.reshape(batch, n)[:, oracle.rev_table(chain, n)]).ravel()
+    assert _d(b_dr) == rec["b_dr"]
+    mr = 16 if v16 else 8
+    assert _d(oracle.conv_foursteps(a, b_dr, n, r_out, mid, mr)) == rec["four"]
+    assert _d(oracle.conv_monolithic(a, b_dr, n, r_out, mid, mr)) == rec["mono"]
+
+
+def test_small_case_arrays_match_digests():
+    g = np.load(os.path.join(GOLD, "reference_cases.npz"))
+    for k in g.files:
+        case, name = k.rsplit("/", 1)
+        assert _d(g[k]) == DIG[case][name], k
