@@ -1,0 +1,327 @@
+"""Benchmark of the fused FFT convolution (BASELINE.json metric):
+"fused conv Gpoints/s + HBM GB/s (% of B200 peak) at N=4096 fp32 & int16-BFP".
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (BASELINE.json configs[1] at N=4096): batch = 2^27/N transforms, so
+the fp32 signal is 1 GiB (the int16-BFP run uses the same point count);
+signal iid N(0,1) complex, filter taps iid U[-1,1) complex turned into a
+spectrum (x 1/N) on the device by this library's own forward transform, one
+filter per transform, mid-op multiply.  A step is one fused-convolution
+launch over the whole batch.  Inputs are 3 GiB per step (1 GiB each for
+signal, filter, result), far above the 126 MB L2, so no flush is needed.
+
+value: device-resident Gpoints/s (points = batch * N), timed with CUDA events
+on the launching stream, max over ranks.  e2e: the same metric through the
+public API with pinned host buffers, host->device and device->host copies in
+the timed region.  roofline: algorithmic bytes (24 B/pt fp32, 12 B/pt BFP)
+per launch over the measured launch time, against the measured HBM copy
+bandwidth.  --gpus N > 1 (under torchrun): every rank runs its own full batch
+(batch sharding, no collective on the data path): weak scaling.
+--impl reference: the reference's own CPU transcription (oracle/_ref,
+compiled from its sources; else the oracle restatement) on all host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N = 4096
+POINTS = 1 << 27
+BYTES_F32 = 24      # read signal 8 + read filter 8 + write result 8 per point
+BYTES_BFP = 12      # the same three streams at 4 B per point (+3 scales per transform)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic(key):
+    """dram bytes per launch from a committed ncu capture (profiles/traffic.json)"""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(key)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled while the timed loop runs"""
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        sm = [float(r[0]) for r in self.rows if len(r) >= 7 and r[0].replace(".", "").isdigit()]
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) >= 7 for i in range(4) if r[3 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(float(r[1]) for r in self.rows if len(r) >= 7),
+                "reasons": reasons, "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------
+def cpu_reference_rate(seconds: float, threads: int | None = None, n: int = N):
+    """The reference's CPU path (kernel_pipeline_v16, verify_kernel.cpp:1051) on a
+    bounded sample: `threads` host threads, each on its own slice of transforms.
+    Returns (points/s, kind, threads, sample description)."""
+    import ctypes as ct
+    import numpy as np
+    from oracle import oracle as orc
+    threads = threads or os.cpu_count() or 1
+    try:
+        ref = orc.Reference()
+        fn, kind = ref.L.ref_pipeline_v16, "reference"
+        args_of = lambda a, b, o, bt: (n, 1, a.ctypes.data, b.ctypes.data, o.ctypes.data, bt)   # noqa: E731
+    except Exception:
+        o_ = orc.Oracle()
+        fn, kind = o_.L.orc_conv, "port"
+        args_of = lambda a, b, o, bt: (n, 16, 1, a.ctypes.data, b.ctypes.data, o.ctypes.data, bt, n)  # noqa: E731
+    rng = np.random.default_rng(7)
+    # calibrate one transform, then size each thread's slice to ~seconds of work
+    a1 = (rng.standard_normal(n) + 1j * rng.standard_normal(n)).astype(np.complex64)
+    b1 = (rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)).astype(np.complex64) / n
+    o1 = np.empty_like(a1)
+    t0 = time.perf_counter()
+    fn(*args_of(a1, b1, o1, 1))
+    per = max(time.perf_counter() - t0, 1e-5)
+    per_thread = max(1, int(seconds / per))
+    bufs = []
+    for _ in range(threads):
+        a = np.tile(a1, per_thread)
+        b = np.tile(b1, per_thread)
+        bufs.append((a, b, np.empty_like(a)))
+    def work(i):
+        a, b, o = bufs[i]
+        fn(*args_of(a, b, o, per_thread))
+    ths = [threading.Thread(target=work, args=(i,)) for i in range(threads)]
+    t0 = time.perf_counter()
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+    dt = time.perf_counter() - t0
+    pts = threads * per_thread * n
+    return pts / dt, kind, threads, f"{threads} threads x {per_thread} transforms of N={n} ({pts} points, {dt:.1f} s)"
+
+
+# ------------------------------------------------------------------------------------------
+def make_inputs(ops, torch, n, batch, seed, device):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    a = torch.randn(batch * n, dtype=torch.complex64, device=device, generator=g)
+    taps = torch.complex(torch.rand(batch * n, device=device, generator=g) * 2 - 1,
+                         torch.rand(batch * n, device=device, generator=g) * 2 - 1)
+    spec = ops.fwd(taps, n, ops.LAYOUT_R16)           # chain order, radix-16
+    spec.mul_(1.0 / n)
+    del taps
+    # chain order -> register-boundary layout: bperm[L + k*T] = chain[16 L + k]
+    bperm = spec.view(batch, n // 16, 16).transpose(1, 2).contiguous().view(-1)
+    return a, spec, bperm
+
+
+def time_steps(torch, fn, steps, warmup, dist):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        fn()
+    e1.record(st)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = e0.elapsed_time(e1) / steps
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def run_ours(args, rank, world, dist):
+    import torch
+    from fufft_b200 import ops
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    ops.init()
+    n = args.n
+    batch = POINTS // n
+    hbm, peak_kind = peaks()
+    a, spec, bperm = make_inputs(ops, torch, n, batch, 1000 * 2 + n + rank, dev)
+    out = torch.empty_like(a)
+    layout = ops.LAYOUT_R16_BPERM
+
+    # ---- fp32 fused conv, device resident
+    launches0 = ops.launch_count()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ms = time_steps(torch, lambda: ops.conv(a, bperm, n, layout, ops.MID_MULTIPLY, out=out),
+                        args.steps, args.warmup, dist)
+    launches = (ops.launch_count() - launches0) // (args.steps + args.warmup) * args.steps
+    pts = batch * n
+    gpts = pts / (ms * 1e-3) / 1e9
+    achieved = BYTES_F32 * pts / (ms * 1e-3) / 1e9
+
+    # ---- int16 BFP fused conv (same points, the reference's linear filter layout)
+    aq, as_ = ops.bfp_pack(a, n)
+    bq, bs = ops.bfp_pack(spec, n)
+    ms_bfp = time_steps(torch, lambda: ops.conv_bfp(aq, as_, bq, bs, n, ops.LAYOUT_R16, ops.MID_MULTIPLY),
+                        args.steps, args.warmup, dist)
+    gpts_bfp = pts / (ms_bfp * 1e-3) / 1e9
+    ach_bfp = (BYTES_BFP * pts + 12 * batch) / (ms_bfp * 1e-3) / 1e9
+    del aq, bq
+
+    # ---- e2e through the public API with pinned host buffers
+    e2e_steps = max(1, min(args.steps, 5))
+    ha = a.cpu().pin_memory()
+    hb = bperm.cpu().pin_memory()
+    ho = torch.empty_like(ha).pin_memory()
+
+    def e2e_step():
+        da = ha.to(dev, non_blocking=True)
+        db = hb.to(dev, non_blocking=True)
+        r = ops.conv(da, db, n, layout, ops.MID_MULTIPLY)
+        ho.copy_(r, non_blocking=True)
+
+    ms_e2e = time_steps(torch, e2e_step, e2e_steps, 1, dist)
+    world_pts = pts * world
+    line = {
+        "metric": "fused conv Gpoints/s + HBM GB/s (% of B200 peak) at N=4096 fp32 & int16-BFP",
+        "value": round(world_pts / (ms * 1e-3) / 1e9, 3),
+        "unit": "Gpoints/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded: signal N(0,1), filter taps U[-1,1) -> spectrum/N)",
+        "config": {"workload": f"configs[1] fused fp32 cyclic conv N={n}, batch={batch} per GPU "
+                               f"(1 GiB signal), one filter per transform, mid-op multiply, "
+                               f"filter in the radix-16 register-boundary layout",
+                   "n": n, "batch_per_gpu": batch, "layout": "R16_BPERM", "parallelism": f"batch-sharded x{world}",
+                   "l2": "inputs 3 GiB per step > 126 MB L2 (no flush needed)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
+                     "traffic": profile_traffic(f"conv_f32_r16_bperm_n{n}"),
+                     "bytes_per_point": BYTES_F32, "kernel": f"conv_kernel<{n},16,...,MUL,SMEM> (1 launch/step)"},
+        "bfp": {"value": round(gpts_bfp * world, 3), "unit": "Gpoints/s", "ms_per_step": round(ms_bfp, 4),
+                "roofline": {"bound": "hbm", "achieved": round(ach_bfp, 1), "peak": hbm, "unit": "GB/s",
+                             "frac": round(ach_bfp / hbm, 4), "bytes_per_point": BYTES_BFP,
+                             "traffic": profile_traffic(f"conv_bfp_r16_n{n}")},
+                "layout": "R16 (the reference's linear mixedrev16 order)"},
+        "e2e": {"value": round(world_pts / (ms_e2e * 1e-3) / 1e9, 3), "unit": "Gpoints/s",
+                "h2d_bytes_per_step": int(ha.numel() * 8 + hb.numel() * 8),
+                "d2h_bytes_per_step": int(ho.numel() * 8), "steps": e2e_steps,
+                "ms_per_step": round(ms_e2e, 3)},
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+    }
+    del ha, hb, ho
+    if rank == 0 and not args.no_cpu_baseline:
+        rate, kind, cores, sample = cpu_reference_rate(args.cpu_seconds)
+        line["cpu_baseline"] = {"value": round(rate / 1e9, 6), "unit": "Gpoints/s", "cores": cores,
+                                "kind": kind, "sample": sample}
+    return line
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    # each step: a bounded sample of the workload on every host core
+    rates = []
+    kind = cores = sample = None
+    for i in range(args.warmup + args.steps):
+        rate, kind, cores, sample = cpu_reference_rate(args.ref_seconds)
+        if i >= args.warmup:
+            rates.append(rate)
+    v = statistics.median(rates) / 1e9
+    return {
+        "metric": "fused conv Gpoints/s + HBM GB/s (% of B200 peak) at N=4096 fp32 & int16-BFP",
+        "impl": "reference", "value": round(v, 6), "unit": "Gpoints/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"configs[1] fused fp32 cyclic conv N={args.n} on host cores "
+                               "(the reference's CPU transcription kernel_pipeline_v16)", "n": args.n},
+        "cpu_baseline": {"value": round(v, 6), "unit": "Gpoints/s", "cores": cores, "kind": kind, "sample": sample},
+        "e2e": {"value": round(v, 6), "unit": "Gpoints/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--n", type=int, default=N)
+    ap.add_argument("--cpu-seconds", type=float, default=2.0, help="per-thread CPU baseline sample")
+    ap.add_argument("--ref-seconds", type=float, default=1.0, help="per-thread sample per reference step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    dist = None
+    if world > 1 and args.impl == "ours":
+        import datetime
+        import torch
+        import torch.distributed as td
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist = td
+    try:
+        line = run_reference(args, rank, world) if args.impl == "reference" else run_ours(args, rank, world, dist)
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,413 @@
+// fufft_conv.cuh -- the fused one-block FFT convolution engine for sm_100a.
+//
+// One CTA runs CPB independent transforms of N points, T = N/R threads each,
+// every thread holding R complex values in registers (R = 16: the V=16 form of
+// fufft.cuh:763-800 / :1448-1497; R = 8: the radix-8 form of :930-1036).
+// The radix chain is the reference's, so spectra come out in the same
+// chain-reversed order and the filter layouts are interchangeable with it:
+//     N = LEAD * R^NR, DIF passes [LEAD (if > 1), R, ..., R], strides
+//     N/LEAD, N/(LEAD R), ..., 1; DIT in reverse.
+//
+// What is B200-specific:
+//   * the first DIF pass reads its taps straight from HBM into registers
+//     (thread `lane` needs a[lane + T*u], u < R: every warp load is one
+//     coalesced 256-byte request), and the last DIT pass stores straight back
+//     the same way -- no shared-memory staging of signal or result;
+//   * the M == 1 passes of forward and inverse meet in registers: spectrum,
+//     filter multiply and inverse butterfly never touch shared memory;
+//   * the filter, in the register-boundary layout, is prefetched with one TMA
+//     bulk copy per transform (cp.async.bulk + mbarrier) at kernel start, so
+//     its HBM latency hides under the forward transform;
+//   * exchanges between passes go through a swizzled shared buffer that is
+//     1-way for every pattern (see swz()); 128-bit at the register boundary;
+//   * twiddles come from fp64-accurate per-stride tables (L1-resident), not
+//     from sincos recurrences;
+//   * every wait is bounded (mbar_wait) and reports through the status word.
+#pragma once
+#include "fufft_device.cuh"
+
+#include <utility>
+
+namespace fufft {
+
+enum class In { C32, BFP, REAL2, SPEC };   // signal form entering the kernel
+enum class Out { C32, BFP, REAL2, SPEC };  // result form leaving it
+enum class Mid { NONE, MUL, CONJ };        // pointwise operation between the transforms
+enum class Flt { NONE, SMEM, GLOBAL };     // filter read: TMA-staged register-boundary
+                                           // layout, or chain order straight from HBM
+
+__host__ __device__ constexpr int ilog2c(long long n) { return n <= 1 ? 0 : 1 + ilog2c(n / 2); }
+
+template<int N_, int R_> struct Chain {
+   static constexpr int N = N_, R = R_;
+   static constexpr int LOGN = ilog2c(N), LOGR = ilog2c(R);
+   static constexpr int NR = LOGN / LOGR;
+   static constexpr int LEAD = 1 << (LOGN % LOGR);
+   static constexpr int NP = NR + (LEAD > 1 ? 1 : 0);
+   static constexpr int T = N / R;
+   __host__ __device__ static constexpr int radix(int p) { return (LEAD > 1 && p == 0) ? LEAD : R; }
+   __host__ __device__ static constexpr int stride(int p)
+   {
+      int M = N;
+      for(int q = 0; q <= p; ++q) M /= radix(q);
+      return M;
+   }
+   static_assert((1 << LOGN) == N && (1 << LOGR) == R, "powers of two only");
+   static_assert(NR >= 1, "the transform must hold at least one full radix-R pass");
+};
+
+struct ConvArgs {
+   const void* a;          // signal: float2 (C32), packed int16 pairs (BFP), float xr (REAL2), spectrum (SPEC)
+   const void* a2;         // REAL2: yr
+   const float* a_scale;   // BFP: one scale per transform
+   const void* b;          // filter spectrum (float2, or packed int16 pairs for BFP)
+   const float* b_scale;   // BFP filter scales
+   void* out;              // result (float2 / packed int16 / ur / spectrum)
+   void* out2;             // REAL2: vr
+   float* out_scale;       // BFP: one scale per transform
+   long long filter_stride;  // elements between consecutive transforms' filters; 0 = one shared filter
+   long long spec_stride;    // SPEC input: elements between consecutive transforms' spectra
+   long long batch;
+   const float2* tw;         // the device's twiddle tables (tw_offset layout)
+   unsigned int* status;     // device status word (bounded-wait reports)
+};
+
+// ---------------------------------------------------------------------------
+// per-pass index maps.  In pass p (radix r, stride M, G = R/r groups per
+// thread) thread `lane` owns groups g = lane + s*T; group g = (b, j) =
+// (g / M, g % M) holds taps b*r*M + j + k*M.  Register x[s*r + k] is tap k of
+// group s.
+// ---------------------------------------------------------------------------
+template<class C, int p, class F>
+__device__ __forceinline__ void visit(int lane, F&& f)
+{
+   constexpr int r = C::radix(p), M = C::stride(p), G = C::R / r, T = C::T;
+#pragma unroll
+   for(int s = 0; s < G; ++s) {
+      const int g = lane + s * T;
+      const int j = g & (M - 1);
+      const int b = g >> ilog2c(M);
+      const int base = b * r * M + j;
+#pragma unroll
+      for(int k = 0; k < r; ++k) f(s * r + k, base + k * M);
+   }
+}
+
+// DIF (S = -1): butterfly, then W^{jk}.  DIT (S = +1): conj(W^{jk}), then butterfly.
+template<class C, int p, int S>
+__device__ __forceinline__ void butterflies(float2 (&x)[C::R], int lane, const float2* __restrict__ twt)
+{
+   constexpr int r = C::radix(p), M = C::stride(p), G = C::R / r, T = C::T;
+#pragma unroll
+   for(int s = 0; s < G; ++s) {
+      float2* u = x + s * r;
+      if constexpr(M > 1) {
+         const float2* tw = twt + tw_offset(r, M) + ((lane + s * T) & (M - 1));
+         if constexpr(S > 0) {
+#pragma unroll
+            for(int k = 1; k < r; ++k) u[k] = cmulc(u[k], __ldca(tw + k * M));
+         }
+         dft<r, S>(u);
+         if constexpr(S < 0) {
+#pragma unroll
+            for(int k = 1; k < r; ++k) u[k] = cmul(u[k], __ldca(tw + k * M));
+         }
+      } else {
+         dft<r, S>(u);
+      }
+   }
+}
+
+// exchange through the swizzled shared buffer; `off` = slot * N
+template<class C, int p>
+__device__ __forceinline__ void xstore(float2* X, int off, const float2 (&x)[C::R], int lane)
+{
+   if constexpr(C::stride(p) == 1) {
+      const int base = off + lane * C::R;
+#pragma unroll
+      for(int k = 0; k < C::R; k += 2)
+         *reinterpret_cast<float4*>(X + swz(base + k)) = make_float4(x[k].x, x[k].y, x[k + 1].x, x[k + 1].y);
+   } else {
+      visit<C, p>(lane, [&](int i, int pos) { X[swz(off + pos)] = x[i]; });
+   }
+}
+
+template<class C, int p>
+__device__ __forceinline__ void xload(const float2* X, int off, float2 (&x)[C::R], int lane)
+{
+   if constexpr(C::stride(p) == 1) {
+      const int base = off + lane * C::R;
+#pragma unroll
+      for(int k = 0; k < C::R; k += 2) {
+         const float4 v = *reinterpret_cast<const float4*>(X + swz(base + k));
+         x[k] = make_float2(v.x, v.y);
+         x[k + 1] = make_float2(v.z, v.w);
+      }
+   } else {
+      visit<C, p>(lane, [&](int i, int pos) { x[i] = X[swz(off + pos)]; });
+   }
+}
+
+// compiler-level ordering point between passes.  (The twiddle tables are
+// read with coherent ld.global.ca rather than the read-only path: ptxas may
+// move read-only loads across bar.sync, and hoisting every later pass's
+// twiddles to the top of the kernel costs ~60 registers and spills.)
+__device__ __forceinline__ void sched_fence() { asm volatile("" ::: "memory"); }
+
+
+// barrier over the T threads of one transform
+template<int T, int CPB>
+__device__ __forceinline__ void slot_sync(int slot)
+{
+   if constexpr(T <= 32) __syncwarp();
+   else if constexpr(CPB == 1) __syncthreads();
+   else asm volatile("bar.sync %0, %1;" :: "r"(slot + 1), "n"(T) : "memory");
+}
+
+// int16 pair <-> fp32 complex, the reference's BFP element (fufft.cuh:1572-1612)
+__device__ __forceinline__ float2 bfp_dequant(uint32_t w, float scale)
+{
+   return make_float2((float)(short)(w & 0xffffu) * scale, (float)(short)(w >> 16) * scale);
+}
+__device__ __forceinline__ uint32_t bfp_quant(float2 v, float inv)
+{
+   const int qx = __float2int_rn(fminf(fmaxf(v.x * inv, -32767.0f), 32767.0f));
+   const int qy = __float2int_rn(fminf(fmaxf(v.y * inv, -32767.0f), 32767.0f));
+   return ((uint32_t)(uint16_t)qy << 16) | (uint16_t)qx;
+}
+
+template<int N, int R, int CPB, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>
+struct ConvKernel {
+   using C = Chain<N, R>;
+   static constexpr int T = C::T;
+   static constexpr int THREADS = CPB * T;
+   static constexpr bool HAS_FILTER = (MID != Mid::NONE) && (OUT != Out::SPEC);
+   static constexpr int FELEM = FBFP ? 4 : 8;
+   static constexpr size_t X_BYTES = (size_t)CPB * N * sizeof(float2);
+   static constexpr size_t F_BYTES = (HAS_FILTER && FLT == Flt::SMEM) ? (size_t)CPB * N * FELEM : 0;
+   static constexpr size_t SMEM = X_BYTES + F_BYTES;
+
+   template<int p>
+   __device__ __forceinline__ static void fwd_step(float2* X, int off, float2 (&x)[R], int lane, int slot,
+                                                   const float2* tw)
+   {
+      sched_fence();
+      if constexpr(p > 0) {
+         xstore<C, p - 1>(X, off, x, lane);
+         slot_sync<T, CPB>(slot);
+         xload<C, p>(X, off, x, lane);
+      }
+      butterflies<C, p, -1>(x, lane, tw);
+   }
+   template<int p>
+   __device__ __forceinline__ static void inv_step(float2* X, int off, float2 (&x)[R], int lane, int slot,
+                                                   const float2* tw)
+   {
+      // p runs NP-1 .. 0
+      sched_fence();
+      if constexpr(p < C::NP - 1) {
+         xstore<C, p + 1>(X, off, x, lane);
+         slot_sync<T, CPB>(slot);
+         xload<C, p>(X, off, x, lane);
+      }
+      butterflies<C, p, +1>(x, lane, tw);
+   }
+   template<int... ps>
+   __device__ __forceinline__ static void fwd_all(float2* X, int off, float2 (&x)[R], int lane, int slot,
+                                                  const float2* tw, std::integer_sequence<int, ps...>)
+   {
+      (fwd_step<ps>(X, off, x, lane, slot, tw), ...);
+   }
+   template<int... ps>
+   __device__ __forceinline__ static void inv_all(float2* X, int off, float2 (&x)[R], int lane, int slot,
+                                                  const float2* tw, std::integer_sequence<int, ps...>)
+   {
+      (inv_step<C::NP - 1 - ps>(X, off, x, lane, slot, tw), ...);
+   }
+
+   __device__ __forceinline__ static void run(const ConvArgs& args)
+   {
+      extern __shared__ __align__(1024) unsigned char smem_raw[];
+      __shared__ uint64_t fbar;
+      __shared__ float warp_max[THREADS / 32 > 0 ? THREADS / 32 : 1];
+      float2* X = reinterpret_cast<float2*>(smem_raw);
+      unsigned char* F = smem_raw + X_BYTES;
+
+      const int slot = threadIdx.x / T, lane = threadIdx.x % T;
+      const long long tr0 = (long long)blockIdx.x * CPB;
+      const long long tr = tr0 + slot;
+      const bool active = tr < args.batch;
+      const int off = slot * N;
+      const size_t gbase = (size_t)tr * N;
+
+      // ---- filter prefetch: one bulk copy per transform, completes on fbar
+      if constexpr(HAS_FILTER && FLT == Flt::SMEM) {
+         if(threadIdx.x == 0) {
+            mbar_init(&fbar, 1);
+            fence_mbar_init();
+         }
+         __syncthreads();
+         if(threadIdx.x == 0) {
+            const long long left = args.batch - tr0;
+            const int nact = left < CPB ? (int)left : CPB;
+            mbar_expect_tx(&fbar, (uint32_t)(nact * N * FELEM));
+            const unsigned char* fb = static_cast<const unsigned char*>(args.b);
+            for(int s = 0; s < nact; ++s)
+               bulk_g2s(F + (size_t)s * N * FELEM, fb + (size_t)((tr0 + s) * args.filter_stride) * FELEM,
+                        (uint32_t)(N * FELEM), &fbar);
+         }
+      }
+
+      float2 x[R];
+
+      if constexpr(IN != In::SPEC) {
+         // ---- first DIF pass straight from HBM: x[s*r + k] = a[lane + T*(s + G*k)]
+         constexpr int r0 = C::radix(0), G0 = R / r0;
+         float sa = 1.0f;
+         if constexpr(IN == In::BFP) sa = active ? __ldg(args.a_scale + tr) : 0.0f;
+#pragma unroll
+         for(int s = 0; s < G0; ++s)
+#pragma unroll
+            for(int k = 0; k < r0; ++k) {
+               const size_t gi = gbase + lane + (size_t)T * (s + G0 * k);
+               float2 v = make_float2(0.f, 0.f);
+               if(active) {
+                  if constexpr(IN == In::C32) v = ld_stream(static_cast<const float2*>(args.a) + gi);
+                  else if constexpr(IN == In::BFP)
+                     v = bfp_dequant(ld_stream(static_cast<const uint32_t*>(args.a) + gi), sa);
+                  else v = make_float2(ld_stream(static_cast<const float*>(args.a) + gi),
+                                       ld_stream(static_cast<const float*>(args.a2) + gi));
+               }
+               x[s * r0 + k] = v;
+            }
+         fwd_all(X, off, x, lane, slot, args.tw, std::make_integer_sequence<int, C::NP>{});
+      } else {
+         // ---- split apply: the chain-order spectrum enters at the boundary
+         const float4* sp = reinterpret_cast<const float4*>(static_cast<const float2*>(args.a) +
+                                                            (size_t)(tr * args.spec_stride) + (size_t)lane * R);
+#pragma unroll
+         for(int k = 0; k < R; k += 2) {
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if(active) v = ld_stream4(sp + k / 2);
+            x[k] = make_float2(v.x, v.y);
+            x[k + 1] = make_float2(v.z, v.w);
+         }
+      }
+
+      // ---- register boundary: x[k] is the spectrum at chain position R*lane + k
+      if constexpr(OUT == Out::SPEC) {
+         if(active) {
+            float4* sp = reinterpret_cast<float4*>(static_cast<float2*>(args.out) + gbase + (size_t)lane * R);
+#pragma unroll
+            for(int k = 0; k < R; k += 2) st_stream(sp + k / 2, make_float4(x[k].x, x[k].y, x[k + 1].x, x[k + 1].y));
+         }
+         return;
+      } else {
+         if constexpr(MID != Mid::NONE) {
+            float2 f[R];
+            if constexpr(FLT == Flt::SMEM) {
+               mbar_wait(&fbar, 0, args.status);
+               if constexpr(FBFP) {
+                  const uint32_t* Fs = reinterpret_cast<const uint32_t*>(F) + off;
+                  const float sb = active ? __ldg(args.b_scale + (args.filter_stride ? tr : 0)) : 0.0f;
+#pragma unroll
+                  for(int k = 0; k < R; ++k) f[k] = bfp_dequant(Fs[lane + k * T], sb);
+               } else {
+                  const float2* Fs = reinterpret_cast<const float2*>(F) + off;
+#pragma unroll
+                  for(int k = 0; k < R; ++k) f[k] = Fs[lane + k * T];
+               }
+            } else {
+               const size_t fbase = (size_t)(tr * args.filter_stride) + (size_t)lane * R;
+               if constexpr(FBFP) {
+                  const float sb = active ? __ldg(args.b_scale + (args.filter_stride ? tr : 0)) : 0.0f;
+                  const uint4* fp = reinterpret_cast<const uint4*>(static_cast<const uint32_t*>(args.b) + fbase);
+#pragma unroll
+                  for(int k = 0; k < R; k += 4) {
+                     uint4 w = make_uint4(0, 0, 0, 0);
+                     if(active) w = __ldg(fp + k / 4);
+                     f[k] = bfp_dequant(w.x, sb); f[k + 1] = bfp_dequant(w.y, sb);
+                     f[k + 2] = bfp_dequant(w.z, sb); f[k + 3] = bfp_dequant(w.w, sb);
+                  }
+               } else {
+                  const float4* fp = reinterpret_cast<const float4*>(static_cast<const float2*>(args.b) + fbase);
+#pragma unroll
+                  for(int k = 0; k < R; k += 2) {
+                     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                     if(active) v = __ldg(fp + k / 2);
+                     f[k] = make_float2(v.x, v.y);
+                     f[k + 1] = make_float2(v.z, v.w);
+                  }
+               }
+            }
+#pragma unroll
+            for(int k = 0; k < R; ++k) x[k] = (MID == Mid::MUL) ? cmul(x[k], f[k]) : cmulc(x[k], f[k]);
+         }
+
+         inv_all(X, off, x, lane, slot, args.tw, std::make_integer_sequence<int, C::NP>{});
+
+         // ---- last DIT pass straight to HBM at the first pass's positions
+         constexpr int r0 = C::radix(0), G0 = R / r0;
+         if constexpr(OUT == Out::BFP) {
+            float m = 0.0f;
+#pragma unroll
+            for(int i = 0; i < R; ++i) m = fmaxf(m, fmaxf(fabsf(x[i].x), fabsf(x[i].y)));
+            if constexpr(T >= 32) {
+#pragma unroll
+               for(int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+               if((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+               slot_sync<T, CPB>(slot);
+               m = 0.0f;
+#pragma unroll
+               for(int w = 0; w < T / 32; ++w) m = fmaxf(m, warp_max[slot * (T / 32) + w]);
+            } else {
+#pragma unroll
+               for(int o = T / 2; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            }
+            const float mx = fmaxf(m, 1e-30f);
+            const float inv = 32767.0f / mx;
+            if(active) {
+               uint32_t* o = static_cast<uint32_t*>(args.out);
+#pragma unroll
+               for(int s = 0; s < G0; ++s)
+#pragma unroll
+                  for(int k = 0; k < r0; ++k)
+                     st_stream(o + gbase + lane + (size_t)T * (s + G0 * k), bfp_quant(x[s * r0 + k], inv));
+               if(lane == 0) args.out_scale[tr] = mx / 32767.0f;
+            }
+         } else if(active) {
+#pragma unroll
+            for(int s = 0; s < G0; ++s)
+#pragma unroll
+               for(int k = 0; k < r0; ++k) {
+                  const size_t gi = gbase + lane + (size_t)T * (s + G0 * k);
+                  const float2 v = x[s * r0 + k];
+                  if constexpr(OUT == Out::C32) st_stream(static_cast<float2*>(args.out) + gi, v);
+                  else {
+                     st_stream(static_cast<float*>(args.out) + gi, v.x);
+                     st_stream(static_cast<float*>(args.out2) + gi, v.y);
+                  }
+               }
+         }
+      }
+   }
+};
+
+// occupancy target: FUFFT_RESIDENT_THREADS per SM (512 = two 256-thread CTAs,
+// which leaves ptxas 128 registers per thread: no spills in any variant)
+#ifndef FUFFT_RESIDENT_THREADS
+#define FUFFT_RESIDENT_THREADS 512
+#endif
+template<int THREADS> constexpr int min_blocks()
+{
+   return THREADS >= FUFFT_RESIDENT_THREADS ? 1 : FUFFT_RESIDENT_THREADS / THREADS;
+}
+
+template<int N, int R, int CPB, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>
+__global__ void __launch_bounds__(CPB * (N / R), min_blocks<CPB * (N / R)>())
+conv_kernel(const ConvArgs args)
+{
+   ConvKernel<N, R, CPB, IN, OUT, MID, FLT, FBFP>::run(args);
+}
+
+}  // namespace fufft

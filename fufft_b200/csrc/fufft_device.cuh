@@ -1,0 +1,231 @@
+// fufft_device.cuh -- device building blocks of the fused FFT-convolution
+// kernels for sm_100a: complex fp32 arithmetic, small DFT butterflies, the
+// twiddle tables, the shared-memory swizzle, and the TMA bulk-copy /
+// mbarrier primitives (inline PTX).
+//
+// Conventions (the ones the reference's C++ entry points expose, fufft.cuh):
+//   * forward transforms use W_N = exp(-2 pi i / N) (sign -1), inverse +1,
+//     unnormalised; the 1/N is folded into the filter spectrum by the caller;
+//   * a radix-r DIF pass at stride M over group (b, j) reads taps
+//     b*r*M + j + k*M, runs a natural-order DFT_r, then multiplies output k by
+//     W_{rM}^{jk}; the DIT pass multiplies by the conjugate first, then runs
+//     the inverse DFT_r (fufft.cuh:460-502, :723-750).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fufft {
+
+// ---------------------------------------------------------------------------
+// complex fp32 on float2 = (re, im)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
+__device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+// a * w, two fused products (same rounding shape as the reference's cmul,
+// fufft.cuh:243-261)
+__device__ __forceinline__ float2 cmul(float2 a, float2 w)
+{
+   return make_float2(fmaf(a.x, w.x, -a.y * w.y), fmaf(a.x, w.y, a.y * w.x));
+}
+// a * conj(w)  (fufft.cuh:644-648, MidConjMultiply)
+__device__ __forceinline__ float2 cmulc(float2 a, float2 w)
+{
+   return make_float2(fmaf(a.x, w.x, a.y * w.y), fmaf(a.y, w.x, -a.x * w.y));
+}
+
+// Exact constants of the 16th roots of unity (rounded once from the exact values).
+#define FUFFT_K_R2  0.70710678118654752440f   // cos(pi/4)
+#define FUFFT_K_C16 0.92387953251128673848f   // cos(pi/8)
+#define FUFFT_K_S16 0.38268343236508977173f   // sin(pi/8)
+
+// a * W_4^1 in direction S (S = -1 forward: -i, S = +1 inverse: +i); free
+template<int S> __device__ __forceinline__ float2 rot4(float2 a)
+{
+   return S < 0 ? make_float2(a.y, -a.x) : make_float2(-a.y, a.x);
+}
+// a * W_8^1 = a * (1 + S i)/sqrt2 : two adds, two multiplies
+template<int S> __device__ __forceinline__ float2 rot8(float2 a)
+{
+   return S < 0 ? make_float2(FUFFT_K_R2 * (a.x + a.y), FUFFT_K_R2 * (a.y - a.x))
+                : make_float2(FUFFT_K_R2 * (a.x - a.y), FUFFT_K_R2 * (a.x + a.y));
+}
+// a * W_8^3 = a * (-1 + S i)/sqrt2
+template<int S> __device__ __forceinline__ float2 rot8_3(float2 a)
+{
+   return S < 0 ? make_float2(FUFFT_K_R2 * (a.y - a.x), -FUFFT_K_R2 * (a.x + a.y))
+                : make_float2(-FUFFT_K_R2 * (a.x + a.y), FUFFT_K_R2 * (a.x - a.y));
+}
+// a * W_16^e for the exponents the 4x4 radix-16 needs
+template<int E, int S> __device__ __forceinline__ float2 rot16(float2 a)
+{
+   if constexpr(E == 0) return a;
+   else if constexpr(E == 2) return rot8<S>(a);
+   else if constexpr(E == 4) return rot4<S>(a);
+   else if constexpr(E == 6) return rot8_3<S>(a);
+   else if constexpr(E == 1) return cmul(a, make_float2(FUFFT_K_C16, (float)S * FUFFT_K_S16));
+   else if constexpr(E == 3) return cmul(a, make_float2(FUFFT_K_S16, (float)S * FUFFT_K_C16));
+   else /* E == 9 */ return cmul(a, make_float2(-FUFFT_K_C16, -(float)S * FUFFT_K_S16));
+}
+
+// ---------------------------------------------------------------------------
+// natural-order DFTs on registers, in place: x[k] <- sum_n x[n] W_r^{S n k}
+// ---------------------------------------------------------------------------
+template<int S> __device__ __forceinline__ void dft2(float2* x)
+{
+   const float2 t = x[0];
+   x[0] = cadd(t, x[1]);
+   x[1] = csub(t, x[1]);
+}
+
+template<int S> __device__ __forceinline__ void dft4(float2& a0, float2& a1, float2& a2, float2& a3)
+{
+   const float2 t0 = cadd(a0, a2), t1 = csub(a0, a2);
+   const float2 t2 = cadd(a1, a3), t3 = rot4<S>(csub(a1, a3));
+   a0 = cadd(t0, t2); a2 = csub(t0, t2);
+   a1 = cadd(t1, t3); a3 = csub(t1, t3);
+}
+template<int S> __device__ __forceinline__ void dft4(float2* x) { dft4<S>(x[0], x[1], x[2], x[3]); }
+
+// 8 = 2 x 4: DFT_4 over the even and the odd taps, W_8^k on the odd half,
+// one radix-2 layer: X[k] = E[k] + W8^k O[k], X[k+4] = E[k] - W8^k O[k].
+template<int S> __device__ __forceinline__ void dft8(float2* x)
+{
+   dft4<S>(x[0], x[2], x[4], x[6]);
+   dft4<S>(x[1], x[3], x[5], x[7]);
+   const float2 o1 = rot8<S>(x[3]), o2 = rot4<S>(x[5]), o3 = rot8_3<S>(x[7]);
+   const float2 e0 = x[0], e1 = x[2], e2 = x[4], e3 = x[6], o0 = x[1];
+   x[0] = cadd(e0, o0); x[4] = csub(e0, o0);
+   x[1] = cadd(e1, o1); x[5] = csub(e1, o1);
+   x[2] = cadd(e2, o2); x[6] = csub(e2, o2);
+   x[3] = cadd(e3, o3); x[7] = csub(e3, o3);
+}
+
+// 16 = 4 x 4 with n = n1 + 4 n2, k = k2 + 4 k1:
+//   Y[n1][k2] = DFT_4 over n2 of x[n1 + 4 n2];  Y[n1][k2] *= W16^{n1 k2};
+//   X[k2 + 4 k1] = DFT_4 over n1 of Y[n1][k2].
+template<int S> __device__ __forceinline__ void dft16(float2* x)
+{
+#pragma unroll
+   for(int n1 = 0; n1 < 4; n1++) dft4<S>(x[n1], x[n1 + 4], x[n1 + 8], x[n1 + 12]);
+   x[5] = rot16<1, S>(x[5]);  x[6] = rot16<2, S>(x[6]);  x[7] = rot16<3, S>(x[7]);
+   x[9] = rot16<2, S>(x[9]);  x[10] = rot16<4, S>(x[10]); x[11] = rot16<6, S>(x[11]);
+   x[13] = rot16<3, S>(x[13]); x[14] = rot16<6, S>(x[14]); x[15] = rot16<9, S>(x[15]);
+   // Y[n1][k2] sits at x[n1 + 4 k2]; the radix-4 over n1 for fixed k2 uses
+   // x[4k2 .. 4k2+3] and leaves X[k2 + 4 k1] at x[4 k2 + k1]
+#pragma unroll
+   for(int k2 = 0; k2 < 4; k2++) dft4<S>(x[4 * k2], x[4 * k2 + 1], x[4 * k2 + 2], x[4 * k2 + 3]);
+   float2 y[16];
+#pragma unroll
+   for(int i = 0; i < 16; i++) y[i] = x[i];
+#pragma unroll
+   for(int k2 = 0; k2 < 4; k2++)
+#pragma unroll
+      for(int k1 = 0; k1 < 4; k1++) x[k2 + 4 * k1] = y[4 * k2 + k1];
+}
+
+template<int R, int S> __device__ __forceinline__ void dft(float2* x)
+{
+   static_assert(R == 2 || R == 4 || R == 8 || R == 16, "radix");
+   if constexpr(R == 2) dft2<S>(x);
+   else if constexpr(R == 4) dft4<S>(x);
+   else if constexpr(R == 8) dft8<S>(x);
+   else dft16<S>(x);
+}
+
+// ---------------------------------------------------------------------------
+// twiddle tables: for each radix r in {2,4,8,16} and stride M (r*M <= 2^16)
+// a table tw[k*M + j] = W_{rM}^{jk} = exp(-2 pi i jk / (rM)), k < r, j < M,
+// computed once per device in fp64 and rounded to fp32.  Transposed ([k][j])
+// so that the lanes of a warp, which hold consecutive j, read consecutive
+// addresses.
+// ---------------------------------------------------------------------------
+constexpr int TW_LOG_MAX = 16;                       // largest r*M
+__host__ __device__ constexpr int tw_block(int r) { return (2 << TW_LOG_MAX) - r; }
+__host__ __device__ constexpr int tw_base(int r)
+{
+   return r == 2 ? 0 : r == 4 ? tw_block(2) : r == 8 ? tw_block(2) + tw_block(4)
+                                            : tw_block(2) + tw_block(4) + tw_block(8);
+}
+__host__ __device__ constexpr int tw_offset(int r, int M) { return tw_base(r) + r * (M - 1); }
+constexpr int TW_TOTAL = tw_base(16) + tw_block(16);
+
+// ---------------------------------------------------------------------------
+// shared-memory swizzle: XOR bits 1..3 of the float2 index with a function of
+// bits 4..6/5..7.  A bijection (bits >= 4 are untouched), keeps adjacent
+// pairs together (bit 0 untouched) so the register boundary moves 16 bytes at
+// a time, and is 1-way on every exchange pattern of the radix-16 and radix-8
+// engines (checked by tests/test_smem_audit.py).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int swz(int p) { return p ^ ((((p >> 4) ^ (p >> 5)) & 7) << 1); }
+
+// ---------------------------------------------------------------------------
+// TMA bulk copy + mbarrier (inline PTX, sm_90+ forms valid on sm_100a)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
+{
+   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init()
+{
+   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(smem_u32(bar)), "r"(bytes)
+                : "memory");
+}
+// global -> shared bulk copy; dst, src 16-byte aligned, bytes a multiple of 16
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
+{
+   uint32_t ok;
+   asm volatile("{\n\t.reg .pred p;\n\t"
+                "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                "selp.u32 %0, 1, 0, p;\n\t}"
+                : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+   return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns()
+{
+   uint64_t t;
+   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+   return t;
+}
+
+// bits of the device status word the host reads through fufft_device_status()
+constexpr unsigned STATUS_TMA_TIMEOUT = 1u;   // a bounded mbarrier wait gave up
+
+// Bounded wait: gives up after `limit_ns` (2 s by default) and records it in
+// the status word instead of spinning forever.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* status,
+                                          uint64_t limit_ns = 2000000000ull)
+{
+   if(mbar_try_wait(bar, parity)) return true;
+   const uint64_t t0 = globaltimer_ns();
+   while(!mbar_try_wait(bar, parity)) {
+      if(globaltimer_ns() - t0 > limit_ns) {
+         atomicOr(status, STATUS_TMA_TIMEOUT);
+         return false;
+      }
+   }
+   return true;
+}
+
+// streaming global loads/stores: data read or written once, kept out of L1 so
+// the twiddle tables stay resident
+__device__ __forceinline__ float2 ld_stream(const float2* p) { return __ldcs(p); }
+__device__ __forceinline__ float4 ld_stream4(const float4* p) { return __ldcs(p); }
+__device__ __forceinline__ uint32_t ld_stream(const uint32_t* p) { return __ldcs(reinterpret_cast<const unsigned int*>(p)); }
+__device__ __forceinline__ float ld_stream(const float* p) { return __ldcs(p); }
+__device__ __forceinline__ void st_stream(float2* p, float2 v) { __stcs(p, v); }
+__device__ __forceinline__ void st_stream(float4* p, float4 v) { __stcs(p, v); }
+__device__ __forceinline__ void st_stream(uint32_t* p, uint32_t v) { __stcs(reinterpret_cast<unsigned int*>(p), v); }
+__device__ __forceinline__ void st_stream(float* p, float v) { __stcs(p, v); }
+
+}  // namespace fufft

@@ -1,0 +1,376 @@
+// fufft_runtime.cu -- per-device state, index maps, filter preparation and
+// the int16 block-floating-point pack/unpack kernels of the C ABI.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "fufft_internal.cuh"
+
+namespace fufft {
+
+// twiddle tables (tw_offset layout) and the status word, one copy per device
+__device__ float2 g_twiddle[TW_TOTAL];
+__device__ unsigned int g_status;
+
+// fill every table: entry (r, M, k, j) = exp(-2 pi i jk / (rM)) from fp64
+// sincospi, rounded once to fp32
+__global__ void twiddle_init_kernel()
+{
+   for(int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < TW_TOTAL; idx += gridDim.x * blockDim.x) {
+      int r = 16;
+      if(idx < tw_base(4)) r = 2;
+      else if(idx < tw_base(8)) r = 4;
+      else if(idx < tw_base(16)) r = 8;
+      const int off = idx - tw_base(r);
+      int M = 1;
+      while(r * (2 * M - 1) <= off) M *= 2;   // largest M with r*(M-1) <= off
+      const int e = off - r * (M - 1);         // k*M + j
+      const int k = e / M, j = e % M;
+      const long long L = (long long)r * M;
+      const long long jk = ((long long)j * k) % L;
+      double s, c;
+      sincospi(-2.0 * (double)jk / (double)L, &s, &c);
+      g_twiddle[idx] = make_float2((float)c, (float)s);
+   }
+}
+
+namespace host {
+
+namespace {
+thread_local std::string t_last_error;
+std::atomic<uint64_t> g_launches{0};
+
+struct DevState {
+   std::once_flag once;
+   fufft_status init_status = FUFFT_OK;
+   const float2* tw = nullptr;
+   unsigned int* status = nullptr;
+};
+constexpr int MAX_DEVICES = 64;
+DevState g_dev[MAX_DEVICES];
+
+fufft_status init_device(DevState& d)
+{
+   void* p = nullptr;
+   fufft_status s = check(cudaGetSymbolAddress(&p, g_twiddle));
+   if(s != FUFFT_OK) return s;
+   d.tw = static_cast<const float2*>(p);
+   s = check(cudaGetSymbolAddress(&p, g_status));
+   if(s != FUFFT_OK) return s;
+   d.status = static_cast<unsigned int*>(p);
+   // a private stream keeps the one-time build off the caller's streams
+   cudaStream_t st;
+   s = check(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+   if(s != FUFFT_OK) return s;
+   twiddle_init_kernel<<<256, 256, 0, st>>>();
+   s = check(cudaGetLastError());
+   if(s == FUFFT_OK) s = check(cudaMemsetAsync(d.status, 0, sizeof(unsigned int), st));
+   if(s == FUFFT_OK) s = check(cudaStreamSynchronize(st));
+   cudaStreamDestroy(st);
+   return s;
+}
+}  // namespace
+
+fufft_status cuda_fail(cudaError_t e)
+{
+   t_last_error = cudaGetErrorString(e);
+   return FUFFT_ERR_CUDA;
+}
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+fufft_status device_ctx(DeviceCtx* out)
+{
+   int dev = 0;
+   fufft_status s = check(cudaGetDevice(&dev));
+   if(s != FUFFT_OK) return s;
+   if(dev < 0 || dev >= MAX_DEVICES) return FUFFT_ERR_UNSUPPORTED;
+   DevState& d = g_dev[dev];
+   std::call_once(d.once, [&] { d.init_status = init_device(d); });
+   if(d.init_status != FUFFT_OK) return d.init_status;
+   out->tw = d.tw;
+   out->status = d.status;
+   out->device = dev;
+   return FUFFT_OK;
+}
+
+}  // namespace host
+
+// ---------------------------------------------------------------------------
+// filter permutation: natural-order spectrum -> chain order / register
+// boundary order, per transform
+// ---------------------------------------------------------------------------
+__host__ __device__ inline long long chain_rev_dev(long long idx, const int* w, int p, int m)
+{
+   long long out = 0;
+   int pos = m, op = 0;
+   // digit k (width w[k], MSB-first in idx) lands at the mirrored position
+   for(int k = 0; k < p; k++) {
+      pos -= w[k];
+      const long long d = (idx >> pos) & ((1LL << w[k]) - 1);
+      out |= d << op;
+      op += w[k];
+   }
+   return out;
+}
+
+struct PermPlan {
+   int w[32];
+   int p = 0, m = 0;
+   int v = 1;          // register-boundary width (1 = plain chain order)
+   int T = 1;
+};
+
+static fufft_status make_perm_plan(int n, fufft_layout layout, PermPlan* pl)
+{
+   const int R = host::layout_radix(layout);
+   if(!R) return FUFFT_ERR_INVALID_ARG;
+   int rad[32];
+   const int nrad = fufft_chain(n, R, rad);
+   if(nrad < 0) return FUFFT_ERR_INVALID_SIZE;
+   pl->p = nrad;
+   pl->m = 0;
+   for(int k = 0; k < nrad; k++) {
+      int lw = 0;
+      while((1 << lw) < rad[k]) lw++;
+      pl->w[k] = lw;
+      pl->m += lw;
+   }
+   pl->v = host::layout_bperm(layout) ? R : 1;
+   pl->T = n / pl->v;
+   return FUFFT_OK;
+}
+
+// destination position i -> natural spectrum index
+__host__ __device__ inline long long perm_src(long long i, const PermPlan& pl)
+{
+   long long c = i;   // chain position
+   if(pl.v > 1) {     // bperm[L + k*T] = chain[v*L + k]
+      const long long L = i % pl.T, k = i / pl.T;
+      c = pl.v * L + k;
+   }
+   // chain[c] = spectrum[rev(c)]
+   return chain_rev_dev(c, pl.w, pl.p, pl.m);
+}
+
+__global__ void filter_permute_kernel(const float2* __restrict__ in, float2* __restrict__ out, int n,
+                                      long long total, PermPlan pl)
+{
+   for(long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x; g < total;
+       g += (long long)gridDim.x * blockDim.x) {
+      const long long t = g / n, i = g % n;
+      out[g] = in[t * n + perm_src(i, pl)];
+   }
+}
+
+// ---------------------------------------------------------------------------
+// int16 BFP pack / unpack.  pack = three short launches so any n works:
+//   1) per-transform abs-max into the scale array (atomicMax on the fp32
+//      bits, which order like the values for x >= 0);
+//   2) quantise with inv = 32767 / max(mx, 1e-30);
+//   3) scale = max(mx, 1e-30) / 32767.
+// Same operations and roundings as the reference's host quantiser.
+// ---------------------------------------------------------------------------
+constexpr int BFP_CHUNK = 2048;   // points per block of the abs-max pass
+
+__global__ void bfp_absmax_kernel(const float2* __restrict__ x, unsigned int* __restrict__ mx_bits, int n,
+                                  int blocks_per_tr)
+{
+   const long long t = blockIdx.x / blocks_per_tr;
+   const long long lo = (long long)(blockIdx.x % blocks_per_tr) * BFP_CHUNK;
+   const long long hi = lo + BFP_CHUNK < n ? lo + BFP_CHUNK : n;
+   float m = 0.0f;
+   for(long long i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+      const float2 v = x[t * n + i];
+      m = fmaxf(m, fmaxf(fabsf(v.x), fabsf(v.y)));
+   }
+   for(int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+   if((threadIdx.x & 31) == 0) atomicMax(mx_bits + t, __float_as_uint(m));
+}
+
+__global__ void bfp_quant_kernel(const float2* __restrict__ x, const float* __restrict__ mxv,
+                                 uint32_t* __restrict__ q, int n, long long total)
+{
+   for(long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x; g < total;
+       g += (long long)gridDim.x * blockDim.x) {
+      const float mx = fmaxf(mxv[g / n], 1e-30f);
+      const float inv = 32767.0f / mx;
+      q[g] = bfp_quant(x[g], inv);
+   }
+}
+
+__global__ void bfp_scale_kernel(float* __restrict__ s, long long batch)
+{
+   const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+   if(t < batch) s[t] = fmaxf(s[t], 1e-30f) / 32767.0f;
+}
+
+__global__ void bfp_unpack_kernel(const uint32_t* __restrict__ q, const float* __restrict__ s,
+                                  float2* __restrict__ x, int n, long long total)
+{
+   for(long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x; g < total;
+       g += (long long)gridDim.x * blockDim.x)
+      x[g] = bfp_dequant(q[g], s[g / n]);
+}
+
+}  // namespace fufft
+
+using namespace fufft;
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+const char* fufft_status_string(fufft_status s)
+{
+   switch(s) {
+   case FUFFT_OK: return "ok";
+   case FUFFT_ERR_INVALID_SIZE: return "invalid size: n must be a supported power of two";
+   case FUFFT_ERR_INVALID_BATCH: return "invalid batch";
+   case FUFFT_ERR_MISALIGNED: return "misaligned pointer or stride";
+   case FUFFT_ERR_CUDA: return "CUDA error (see fufft_last_cuda_error)";
+   case FUFFT_ERR_TIMEOUT: return "a bounded device wait timed out";
+   case FUFFT_ERR_PEER_UNAVAILABLE: return "peer device unavailable";
+   case FUFFT_ERR_INVALID_ARG: return "invalid argument";
+   case FUFFT_ERR_UNSUPPORTED: return "unsupported by this build";
+   }
+   return "unknown status";
+}
+
+const char* fufft_last_cuda_error(void) { return host::t_last_error.c_str(); }
+
+int fufft_max_n(fufft_layout layout) { return host::max_n(host::layout_radix(layout)); }
+
+fufft_status fufft_init(void)
+{
+   host::DeviceCtx c;
+   return host::device_ctx(&c);
+}
+
+fufft_status fufft_device_status(uint32_t* status_out, fufft_stream_t stream)
+{
+   if(!status_out) return FUFFT_ERR_INVALID_ARG;
+   host::DeviceCtx c;
+   fufft_status s = host::device_ctx(&c);
+   if(s != FUFFT_OK) return s;
+   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+   unsigned int v = 0;
+   s = host::check(cudaMemcpyAsync(&v, c.status, sizeof(v), cudaMemcpyDeviceToHost, st));
+   if(s == FUFFT_OK) s = host::check(cudaMemsetAsync(c.status, 0, sizeof(unsigned int), st));
+   if(s == FUFFT_OK) s = host::check(cudaStreamSynchronize(st));
+   *status_out = v;
+   return s;
+}
+
+uint64_t fufft_launch_count(void) { return host::g_launches.load(); }
+
+int fufft_chain(int n, int radix, int* radices_out)
+{
+   if(!host::pow2(n) || !host::pow2(radix) || radix < 2 || !radices_out) return -1;
+   int m = 0, rb = 0;
+   while((1 << m) < n) m++;
+   while((1 << rb) < radix) rb++;
+   const int nr = m / rb, lead = 1 << (m % rb);
+   int p = 0;
+   if(lead > 1) radices_out[p++] = lead;
+   for(int i = 0; i < nr && p < 32; i++) radices_out[p++] = radix;
+   return p;
+}
+
+int64_t fufft_chain_rev(int64_t idx, const int* radices, int nrad)
+{
+   if(!radices || nrad < 0 || nrad > 32) return -1;
+   int w[32], m = 0;
+   for(int k = 0; k < nrad; k++) {
+      int lw = 0;
+      while((1 << lw) < radices[k]) lw++;
+      w[k] = lw;
+      m += lw;
+   }
+   return chain_rev_dev(idx, w, nrad, m);
+}
+
+fufft_status fufft_filter_permute_host(const float* spec_natural, float* out, int n, int batch,
+                                       fufft_layout layout)
+{
+   if(!spec_natural || !out || spec_natural == out) return FUFFT_ERR_INVALID_ARG;
+   if(batch < 0) return FUFFT_ERR_INVALID_BATCH;
+   if(!host::pow2(n)) return FUFFT_ERR_INVALID_SIZE;
+   PermPlan pl;
+   fufft_status s = make_perm_plan(n, layout, &pl);
+   if(s != FUFFT_OK) return s;
+   if(pl.v > 1 && n % pl.v) return FUFFT_ERR_INVALID_SIZE;
+   const float2* in = reinterpret_cast<const float2*>(spec_natural);
+   float2* o = reinterpret_cast<float2*>(out);
+   for(long long i = 0; i < n; i++) {
+      const long long src = perm_src(i, pl);
+      for(long long t = 0; t < batch; t++) o[t * n + i] = in[t * n + src];
+   }
+   return FUFFT_OK;
+}
+
+fufft_status fufft_filter_permute(const float* spec_natural, float* out, int n, int batch,
+                                  fufft_layout layout, fufft_stream_t stream)
+{
+   if(!spec_natural || !out || spec_natural == out) return FUFFT_ERR_INVALID_ARG;
+   if(batch < 0) return FUFFT_ERR_INVALID_BATCH;
+   if(!host::pow2(n)) return FUFFT_ERR_INVALID_SIZE;
+   if(!host::aligned(spec_natural, 8) || !host::aligned(out, 8)) return FUFFT_ERR_MISALIGNED;
+   PermPlan pl;
+   fufft_status s = make_perm_plan(n, layout, &pl);
+   if(s != FUFFT_OK) return s;
+   if(pl.v > 1 && n % pl.v) return FUFFT_ERR_INVALID_SIZE;
+   if(batch == 0) return FUFFT_OK;
+   const long long total = (long long)n * batch;
+   const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+   filter_permute_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const float2*>(spec_natural), reinterpret_cast<float2*>(out), n, total, pl);
+   host::count_launch();
+   return host::check(cudaGetLastError());
+}
+
+fufft_status fufft_bfp_pack(const float* x, int16_t* q, float* scale, int n, int64_t batch,
+                            fufft_stream_t stream)
+{
+   if(!x || !q || !scale) return FUFFT_ERR_INVALID_ARG;
+   if(batch < 0) return FUFFT_ERR_INVALID_BATCH;
+   if(n <= 0) return FUFFT_ERR_INVALID_SIZE;
+   if(!host::aligned(x, 8) || !host::aligned(q, 4) || !host::aligned(scale, 4)) return FUFFT_ERR_MISALIGNED;
+   if(batch == 0) return FUFFT_OK;
+   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+   fufft_status s = host::check(cudaMemsetAsync(scale, 0, sizeof(float) * batch, st));
+   if(s != FUFFT_OK) return s;
+   const int bpt = (n + BFP_CHUNK - 1) / BFP_CHUNK;
+   bfp_absmax_kernel<<<(unsigned)(bpt * batch), 256, 0, st>>>(reinterpret_cast<const float2*>(x),
+                                                            reinterpret_cast<unsigned int*>(scale), n, bpt);
+   const long long total = (long long)n * batch;
+   const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+   bfp_quant_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<const float2*>(x), scale,
+                                            reinterpret_cast<uint32_t*>(q), n, total);
+   bfp_scale_kernel<<<(unsigned)((batch + 255) / 256), 256, 0, st>>>(scale, batch);
+   host::count_launch(); host::count_launch(); host::count_launch();
+   return host::check(cudaGetLastError());
+}
+
+fufft_status fufft_bfp_unpack(const int16_t* q, const float* scale, float* x, int n, int64_t batch,
+                              fufft_stream_t stream)
+{
+   if(!x || !q || !scale) return FUFFT_ERR_INVALID_ARG;
+   if(batch < 0) return FUFFT_ERR_INVALID_BATCH;
+   if(n <= 0) return FUFFT_ERR_INVALID_SIZE;
+   if(!host::aligned(x, 8) || !host::aligned(q, 4) || !host::aligned(scale, 4)) return FUFFT_ERR_MISALIGNED;
+   if(batch == 0) return FUFFT_OK;
+   const long long total = (long long)n * batch;
+   const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+   bfp_unpack_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint32_t*>(q), scale, reinterpret_cast<float2*>(x), n, total);
+   host::count_launch();
+   return host::check(cudaGetLastError());
+}
+
+}  // extern "C"

@@ -1,0 +1,10 @@
+// kernel family: fwd_r8 (split forward, radix-8 chain).  Instantiations of the fused engine (fufft_conv.cuh).
+#include "fufft_internal.cuh"
+namespace fufft {
+namespace host {
+fufft_status family_fwd_r8(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
+{
+   (void)mid; (void)bperm; return launch_n<8, In::C32, Out::SPEC, Mid::NONE, Flt::NONE, false>(n, a, st, dev);
+}
+}  // namespace host
+}  // namespace fufft

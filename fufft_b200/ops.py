@@ -1,0 +1,231 @@
+"""Python mirror of the reference's entry points over the C ABI.
+
+The reference (weiwang217/FuFFT, fufft.cuh) exposes kernel templates that the
+caller launches with a mid-op policy struct; here each becomes a function over
+CUDA tensors that calls the corresponding C entry point on the current torch
+stream.  Names follow the reference:
+
+    pipeline_ip(a, b_dr)        fufft_pipeline_ip   (radix-8 chain, any mid-op)
+    pipeline_fused(a, bperm)    fufft_pipeline_fused (radix-8 register boundary)
+    pipeline_v16(a, b16)        fufft_pipeline_v16  (radix-16 chain)
+    pipeline_v16f(a, bperm16)   fufft_pipeline_v16f (radix-16 register boundary)
+    pipeline_r16(a, b16)        fufft_pipeline_r16  (same math as v16)
+    pipeline_fwd / pipeline_apply   split forward / apply
+    conv_r2                     fufft_conv_r2 (two-for-one real)
+    pipeline_v16_bfp            fufft_pipeline_v16_bfp (int16 BFP)
+
+Complex data: torch.complex64 (or float32 with a trailing dim of 2), one
+transform per row of n points.  int16 BFP data: torch.int16 with a trailing
+dim of 2 (re, im) plus one float32 scale per transform.
+"""
+from __future__ import annotations
+
+import ctypes as ct
+
+import torch
+
+from ._lib import (LAYOUT_NATURAL, LAYOUT_R8, LAYOUT_R8_BPERM, LAYOUT_R16, LAYOUT_R16_BPERM,
+                   MID_CONJ_MULTIPLY, MID_MULTIPLY, MID_NONE, FufftError, check, lib)
+
+__all__ = [
+    "MID_NONE", "MID_MULTIPLY", "MID_CONJ_MULTIPLY",
+    "LAYOUT_R8", "LAYOUT_R8_BPERM", "LAYOUT_R16", "LAYOUT_R16_BPERM", "LAYOUT_NATURAL",
+    "FufftError", "chain", "chain_rev", "filter_permute", "filter_permute_host", "conv", "fwd", "apply",
+    "conv_r2", "bfp_pack", "bfp_unpack", "conv_bfp", "pipeline_ip", "pipeline_fused", "pipeline_v16",
+    "pipeline_v16f", "pipeline_r16", "pipeline_fwd", "pipeline_apply", "pipeline_v16_bfp", "init",
+    "device_status", "launch_count", "max_n",
+]
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None):
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("fufft_b200 operates on CUDA tensors")
+    if not t.is_contiguous():
+        raise ValueError("tensor must be contiguous")
+    return t.data_ptr()
+
+
+def _complex(t: torch.Tensor) -> torch.Tensor:
+    if t.dtype == torch.complex64:
+        return t
+    if t.dtype == torch.float32 and t.shape[-1] == 2:
+        return torch.view_as_complex(t)
+    raise TypeError("complex data must be complex64 (or float32 [..., 2])")
+
+
+def _batch(t: torch.Tensor, n: int, per_point: int = 1) -> int:
+    total = t.numel() // per_point
+    if total % n:
+        raise ValueError(f"{total} points is not a whole number of transforms of {n}")
+    return total // n
+
+
+# ---- library / index maps ---------------------------------------------------
+def init() -> None:
+    check(lib().fufft_init(), "fufft_init")
+
+
+def max_n(layout: int) -> int:
+    return lib().fufft_max_n(layout)
+
+
+def launch_count() -> int:
+    return int(lib().fufft_launch_count())
+
+
+def device_status() -> int:
+    v = ct.c_uint32()
+    check(lib().fufft_device_status(ct.byref(v), _stream()), "fufft_device_status")
+    return v.value
+
+
+def chain(n: int, radix: int) -> list[int]:
+    buf = (ct.c_int * 32)()
+    p = lib().fufft_chain(n, radix, buf)
+    if p < 0:
+        raise ValueError(f"n={n} radix={radix}")
+    return list(buf[:p])
+
+
+def chain_rev(idx: int, radices) -> int:
+    arr = (ct.c_int * len(radices))(*radices)
+    return int(lib().fufft_chain_rev(idx, arr, len(radices)))
+
+
+def filter_permute(spec_natural: torch.Tensor, n: int, layout: int) -> torch.Tensor:
+    """natural-order spectrum (device) -> kernel layout, per transform"""
+    s = _complex(spec_natural).contiguous()
+    out = torch.empty_like(s)
+    check(lib().fufft_filter_permute(_ptr(s), _ptr(out), n, _batch(s, n), layout, _stream()),
+          "fufft_filter_permute")
+    return out
+
+
+def filter_permute_host(spec_natural, n: int, layout: int):
+    """numpy complex64 natural-order spectrum -> kernel layout (host)"""
+    import numpy as np
+    s = np.ascontiguousarray(spec_natural, dtype=np.complex64)
+    out = np.empty_like(s)
+    check(lib().fufft_filter_permute_host(s.ctypes.data, out.ctypes.data, n, s.size // n, layout),
+          "fufft_filter_permute_host")
+    return out
+
+
+# ---- fused convolutions -------------------------------------------------------
+def conv(a: torch.Tensor, b: torch.Tensor | None, n: int, layout: int = LAYOUT_R16_BPERM,
+         mid: int = MID_MULTIPLY, filter_stride: int | None = None,
+         out: torch.Tensor | None = None) -> torch.Tensor:
+    a = _complex(a)
+    bt = None if b is None else _complex(b)
+    out = torch.empty_like(a) if out is None else _complex(out)
+    fs = n if filter_stride is None else filter_stride
+    check(lib().fufft_conv_c2c_f32(_ptr(a), _ptr(bt), _ptr(out), n, _batch(a, n), layout, mid, fs, _stream()),
+          "fufft_conv_c2c_f32")
+    return out
+
+
+def fwd(a: torch.Tensor, n: int, layout: int = LAYOUT_R8) -> torch.Tensor:
+    a = _complex(a)
+    spec = torch.empty_like(a)
+    check(lib().fufft_fwd_f32(_ptr(a), _ptr(spec), n, _batch(a, n), layout, _stream()), "fufft_fwd_f32")
+    return spec
+
+
+def apply(spec: torch.Tensor, b: torch.Tensor | None, n: int, layout: int = LAYOUT_R8,
+          mid: int = MID_MULTIPLY, batch: int | None = None, spec_stride: int | None = None,
+          filter_stride: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    spec = _complex(spec)
+    bt = None if b is None else _complex(b)
+    batch = _batch(spec, n) if batch is None else batch
+    ss = n if spec_stride is None else spec_stride
+    fs = n if filter_stride is None else filter_stride
+    if out is None:
+        out = torch.empty(batch * n, dtype=torch.complex64, device=spec.device)
+    check(lib().fufft_apply_f32(_ptr(spec), _ptr(bt), _ptr(out), n, batch, layout, mid, ss, fs, _stream()),
+          "fufft_apply_f32")
+    return out
+
+
+def conv_r2(xr: torch.Tensor, yr: torch.Tensor, b: torch.Tensor, n: int, layout: int = LAYOUT_R8,
+            mid: int = MID_MULTIPLY, filter_stride: int | None = None):
+    bt = _complex(b)
+    ur, vr = torch.empty_like(xr), torch.empty_like(yr)
+    fs = n if filter_stride is None else filter_stride
+    check(lib().fufft_conv_r2_f32(_ptr(xr), _ptr(yr), _ptr(bt), _ptr(ur), _ptr(vr), n, _batch(xr, n),
+                                  layout, mid, fs, _stream()), "fufft_conv_r2_f32")
+    return ur, vr
+
+
+# ---- int16 block floating point -------------------------------------------------
+def bfp_pack(x: torch.Tensor, n: int):
+    x = _complex(x)
+    batch = _batch(x, n)
+    q = torch.empty(x.numel(), 2, dtype=torch.int16, device=x.device)
+    s = torch.empty(batch, dtype=torch.float32, device=x.device)
+    check(lib().fufft_bfp_pack(_ptr(x), _ptr(q), _ptr(s), n, batch, _stream()), "fufft_bfp_pack")
+    return q, s
+
+
+def bfp_unpack(q: torch.Tensor, s: torch.Tensor, n: int) -> torch.Tensor:
+    batch = _batch(q, n, 2)
+    x = torch.empty(batch * n, dtype=torch.complex64, device=q.device)
+    check(lib().fufft_bfp_unpack(_ptr(q), _ptr(s), _ptr(x), n, batch, _stream()), "fufft_bfp_unpack")
+    return x
+
+
+def conv_bfp(aq: torch.Tensor, a_scale: torch.Tensor, bq: torch.Tensor | None, b_scale: torch.Tensor | None,
+             n: int, layout: int = LAYOUT_R16, mid: int = MID_MULTIPLY, filter_stride: int | None = None):
+    batch = _batch(aq, n, 2)
+    oq = torch.empty_like(aq)
+    os_ = torch.empty(batch, dtype=torch.float32, device=aq.device)
+    fs = n if filter_stride is None else filter_stride
+    check(lib().fufft_conv_c2c_bfp(_ptr(aq), _ptr(a_scale), _ptr(bq), _ptr(b_scale), _ptr(oq), _ptr(os_), n,
+                                   batch, layout, mid, fs, _stream()), "fufft_conv_c2c_bfp")
+    return oq, os_
+
+
+# ---- the reference's entry-point names ----------------------------------------------
+def pipeline_ip(a, b_dr, n, mid=MID_MULTIPLY):
+    """fufft_pipeline_ip<N, LEAD, NR8, CPB, Mid>: radix-8 chain, filter in mixedrev order"""
+    return conv(a, b_dr, n, LAYOUT_R8, mid)
+
+
+def pipeline_fused(a, bperm, n):
+    """fufft_pipeline_fused: radix-8 chain, filter in the register-boundary layout"""
+    return conv(a, bperm, n, LAYOUT_R8_BPERM, MID_MULTIPLY)
+
+
+def pipeline_v16(a, b16, n, mid=MID_MULTIPLY):
+    """fufft_pipeline_v16: radix-16 chain, filter in mixedrev16 order"""
+    return conv(a, b16, n, LAYOUT_R16, mid)
+
+
+def pipeline_v16f(a, bperm16, n):
+    """fufft_pipeline_v16f: radix-16 chain, filter in the register-boundary layout"""
+    return conv(a, bperm16, n, LAYOUT_R16_BPERM, MID_MULTIPLY)
+
+
+def pipeline_r16(a, b16, n, mid=MID_MULTIPLY):
+    """fufft_pipeline_r16: same transform and filter order as pipeline_v16"""
+    return conv(a, b16, n, LAYOUT_R16, mid)
+
+
+def pipeline_fwd(a, n):
+    """fufft_pipeline_fwd: radix-8 chain-order spectrum"""
+    return fwd(a, n, LAYOUT_R8)
+
+
+def pipeline_apply(spec, b_dr, n, mid=MID_MULTIPLY):
+    """fufft_pipeline_apply: spectrum x filter, inverse (radix-8 chain)"""
+    return apply(spec, b_dr, n, LAYOUT_R8, mid)
+
+
+def pipeline_v16_bfp(aq, a_scale, bq, b_scale, n):
+    """fufft_pipeline_v16_bfp: int16 BFP in and out, radix-16 chain"""
+    return conv_bfp(aq, a_scale, bq, b_scale, n, LAYOUT_R16, MID_MULTIPLY)

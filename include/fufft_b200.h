@@ -1,0 +1,171 @@
+/*
+ * fufft_b200.h -- C ABI of the B200-native fused FFT-convolution library.
+ *
+ * The reference (weiwang217/FuFFT) ships header-only CUDA templates that a
+ * caller launches itself (fufft.cuh); this library replaces them with plain
+ * C entry points: raw pointers and sizes, no C++ or torch types, one
+ * cudaStream_t-compatible stream handle, a status code instead of exit().
+ * Each entry point below names the reference interface it replaces.
+ *
+ * Common rules
+ *   - Data pointers are DEVICE pointers owned by the caller, except where a
+ *     function says "host".  Calls are asynchronous on `stream` (NULL = the
+ *     legacy default stream) and keep no per-call state.
+ *   - Complex data are interleaved fp32 pairs (re, im) = float2.  int16
+ *     block-floating-point (BFP) data are packed (re, im) int16 pairs (short2,
+ *     4 bytes per point) plus one fp32 scale per transform: value = q * scale.
+ *   - A transform of n points is stored contiguously; `batch` transforms
+ *     follow each other (transform t starts at element t*n).
+ *   - Filter spectra already carry the 1/n normalisation (the reference's
+ *     convention, bench_fufft.cu:156-165) and are stored in one of the
+ *     fufft_layout orders below.  filter_stride is the element distance
+ *     between the filters of consecutive transforms: n for one filter per
+ *     transform, 0 for a single filter shared by the whole batch.
+ *   - n must be a power of two within the range the layout supports
+ *     (fufft_max_n()); batch >= 0; signal/result pointers 8-byte aligned,
+ *     filter pointers 16-byte aligned.
+ *   - The first call on a device builds that device's twiddle tables
+ *     (a short kernel plus a synchronize); call fufft_init() first if the
+ *     stream might be under graph capture.
+ *   - Thread-safe across host threads, streams and devices.
+ */
+#ifndef FUFFT_B200_H
+#define FUFFT_B200_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#include <stdint.h>
+
+typedef struct CUstream_st* fufft_stream_t; /* same type as cudaStream_t */
+
+typedef enum fufft_status {
+   FUFFT_OK = 0,
+   FUFFT_ERR_INVALID_SIZE = 1,     /* n not a supported power of two */
+   FUFFT_ERR_INVALID_BATCH = 2,    /* batch < 0 */
+   FUFFT_ERR_MISALIGNED = 3,       /* a pointer or stride breaks the alignment rule */
+   FUFFT_ERR_CUDA = 4,             /* a CUDA runtime call failed (fufft_last_cuda_error) */
+   FUFFT_ERR_TIMEOUT = 5,          /* a bounded device wait gave up (fufft_device_status) */
+   FUFFT_ERR_PEER_UNAVAILABLE = 6, /* multi-GPU: a peer device cannot be reached */
+   FUFFT_ERR_INVALID_ARG = 7,      /* null pointer, bad enum value, bad stride */
+   FUFFT_ERR_UNSUPPORTED = 8       /* valid request this build does not implement */
+} fufft_status;
+
+/* Mid-operation between the forward and the inverse transform; the
+ * reference's policy structs MidNothing / MidMultiply / MidConjMultiply
+ * (fufft.cuh:625-650). */
+typedef enum fufft_midop {
+   FUFFT_MID_NONE = 0,          /* round trip: out = n * a */
+   FUFFT_MID_MULTIPLY = 1,      /* convolution: spectrum * filter */
+   FUFFT_MID_CONJ_MULTIPLY = 2  /* correlation: spectrum * conj(filter) */
+} fufft_midop;
+
+/* Filter-spectrum orders.  "Chain order" is the order a DIF transform leaves
+ * its spectrum in: bit-group reversal over the radix widths in pass order
+ * (verify_kernel.cpp:145-156 mixedrev, :946-956 mixedrev16).
+ *   R8 / R16        chain order of the radix-8 / radix-16 chain, linear:
+ *                   filter[i] = spectrum[rev(i)] -- the layout taken by the
+ *                   reference's fufft_pipeline_ip / fufft_pipeline_v16
+ *   R8_BPERM /      the register-boundary layout of fufft_pipeline_fused /
+ *   R16_BPERM       fufft_pipeline_v16f: bperm[L + k*T] = chain[V*L + k],
+ *                   T = n/V, V = 8 / 16 (verify_kernel.cpp:1339-1344, :1382-1387)
+ *   NATURAL         natural frequency order (input to fufft_filter_permute)
+ * The BPERM layouts let the library prefetch the filter with one TMA bulk
+ * copy and are the fastest. */
+typedef enum fufft_layout {
+   FUFFT_LAYOUT_R8 = 0,
+   FUFFT_LAYOUT_R8_BPERM = 1,
+   FUFFT_LAYOUT_R16 = 2,
+   FUFFT_LAYOUT_R16_BPERM = 3,
+   FUFFT_LAYOUT_NATURAL = 4
+} fufft_layout;
+
+/* ---- library ------------------------------------------------------------ */
+const char* fufft_status_string(fufft_status s);
+/* text of the last CUDA error seen by this host thread ("" if none) */
+const char* fufft_last_cuda_error(void);
+/* largest one-kernel n for a layout (R8*: 4096, R16*: 8192) */
+int fufft_max_n(fufft_layout layout);
+/* build the current device's twiddle tables now (otherwise done on first use) */
+fufft_status fufft_init(void);
+/* read and clear the device status word of the current device: bit 0 = a
+ * bounded TMA wait timed out.  Synchronises `stream`. */
+fufft_status fufft_device_status(uint32_t* status_out, fufft_stream_t stream);
+/* number of fused-kernel launches this process has issued (all threads) */
+uint64_t fufft_launch_count(void);
+
+/* ---- index maps (host) -------------------------------------------------- */
+/* radix chain of a one-kernel transform: [lead, R, ..., R]; returns its
+ * length (<= 32) or -1.  Replaces factorise/factorise16 (verify_kernel.cpp:126-139). */
+int fufft_chain(int n, int radix, int* radices_out);
+/* chain-reversed index (verify_kernel.cpp:460-477 chain_rev) */
+int64_t fufft_chain_rev(int64_t idx, const int* radices, int nrad);
+
+/* ---- filter preparation -------------------------------------------------
+ * Natural-order spectrum -> a kernel layout, per transform.  Replaces the
+ * host loops of bench_fufft.cu:166-170 (mixedrev_host) and
+ * verify_kernel.cpp:1339-1344 / :1382-1387 (bperm).
+ * _host: host pointers; the other form: device pointers, async on stream.
+ * in != out. */
+fufft_status fufft_filter_permute_host(const float* spec_natural, float* out, int n, int batch,
+                                       fufft_layout layout);
+fufft_status fufft_filter_permute(const float* spec_natural, float* out, int n, int batch,
+                                  fufft_layout layout, fufft_stream_t stream);
+
+/* ---- fused fp32 convolution ---------------------------------------------
+ * out = IDFT(DFT(a) . mid(filter)) for each transform, one kernel launch,
+ * three HBM streams (signal, filter, result).  a == out is allowed.
+ * Replaces fufft_pipeline_ip (fufft.cuh:1757-1772, layout R8),
+ * fufft_pipeline_fused (:1774-1791, R8_BPERM), fufft_pipeline_v16 / _r16
+ * (:1518-1534, :1736-1755, R16) and fufft_pipeline_v16f (:1499-1516,
+ * R16_BPERM), with any mid-op on every layout.  b may be NULL for
+ * FUFFT_MID_NONE. */
+fufft_status fufft_conv_c2c_f32(const float* a, const float* b, float* out, int n, int64_t batch,
+                                fufft_layout layout, fufft_midop mid, int64_t filter_stride,
+                                fufft_stream_t stream);
+
+/* ---- split forward / apply (one signal, many filters) -------------------
+ * fwd: natural-order signal -> chain-order spectrum (layout R8 or R16 picks
+ * the chain).  Replaces fufft_pipeline_fwd (fufft.cuh:1343-1373).
+ * apply: chain-order spectrum (x) filter -> inverse -> natural order.
+ * Replaces fufft_pipeline_apply (fufft.cuh:1375-1407, multiply only there);
+ * spec_stride is the element distance between consecutive transforms'
+ * spectra (n, or 0 to apply many filters to one spectrum). */
+fufft_status fufft_fwd_f32(const float* a, float* spec, int n, int64_t batch, fufft_layout layout,
+                           fufft_stream_t stream);
+fufft_status fufft_apply_f32(const float* spec, const float* b, float* out, int n, int64_t batch,
+                             fufft_layout layout, fufft_midop mid, int64_t spec_stride,
+                             int64_t filter_stride, fufft_stream_t stream);
+
+/* ---- two-for-one real convolution ---------------------------------------
+ * Two real signals ride one complex transform (xr + i*yr); the filter must be
+ * the spectrum of a REAL filter.  ur = xr (*) h, vr = yr (*) h.
+ * Replaces fufft_conv_r2 (fufft.cuh:1273-1330). */
+fufft_status fufft_conv_r2_f32(const float* xr, const float* yr, const float* b, float* ur, float* vr,
+                               int n, int64_t batch, fufft_layout layout, fufft_midop mid,
+                               int64_t filter_stride, fufft_stream_t stream);
+
+/* ---- int16 block floating point -----------------------------------------
+ * pack: fp32 complex -> int16 pairs + one scale per transform:
+ *   mx = max(|re|,|im|) (>= 1e-30), q = rint(clamp(x * 32767/mx, +-32767)),
+ *   scale = mx / 32767 -- bit-exact with bfp_quant_host (bench_fufft.cu:107-117)
+ *   and bfp_quantize (verify_kernel.cpp:1092-1105).
+ * unpack: q * scale. */
+fufft_status fufft_bfp_pack(const float* x, int16_t* q, float* scale, int n, int64_t batch,
+                            fufft_stream_t stream);
+fufft_status fufft_bfp_unpack(const int16_t* q, const float* scale, float* x, int n, int64_t batch,
+                              fufft_stream_t stream);
+/* fused BFP convolution: dequantise, fp32 transforms, filter mid-op,
+ * per-transform abs-max, requantise.  Replaces fufft_pipeline_v16_bfp
+ * (fufft.cuh:1614-1701; layout R16, filter quantised per transform).  The
+ * filter scale array has one entry per filter (1 when filter_stride == 0). */
+fufft_status fufft_conv_c2c_bfp(const int16_t* aq, const float* a_scale, const int16_t* bq,
+                                const float* b_scale, int16_t* oq, float* o_scale, int n, int64_t batch,
+                                fufft_layout layout, fufft_midop mid, int64_t filter_stride,
+                                fufft_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FUFFT_B200_H */

@@ -1,0 +1,79 @@
+"""Shared-memory audit of the exchange patterns of the fused engine
+(fufft_b200/csrc/fufft_conv.cuh), in the style of the reference's
+audit_smem.py: the swizzle must be a bijection and every exchange access
+1-way (64-bit accesses: 16-lane phases; the 128-bit register-boundary
+accesses: 8-lane phases).  Mirrors swz() and the per-pass thread mapping."""
+import pytest
+
+
+def swz(p):   # fufft_device.cuh swz()
+    return p ^ ((((p >> 4) ^ (p >> 5)) & 7) << 1)
+
+
+def chain(n, r):
+    m, rb = n.bit_length() - 1, r.bit_length() - 1
+    lead = 1 << (m % rb)
+    return ([lead] if lead > 1 else []) + [r] * (m // rb)
+
+
+def passes(n, r):
+    out, M = [], n
+    for q in chain(n, r):
+        M //= q
+        out.append((q, M))
+    return out
+
+
+def positions(n, R, p, lane):
+    r, M = passes(n, R)[p]
+    T, G = n // R, R // r
+    res = []
+    for s in range(G):
+        g = lane + s * T
+        j, b = g % M, g // M
+        res += [b * r * M + j + k * M for k in range(r)]
+    return res
+
+
+def worst_ways(addrs, width):
+    phase = 16 if width == 8 else 8
+    worst = 1
+    for a in range(len(addrs[0])):
+        for p0 in range(0, len(addrs), phase):
+            banks = {}
+            for row in addrs[p0:p0 + phase]:
+                unit = row[a] if width == 8 else row[a] // 2
+                banks.setdefault((unit * width // 4) % 32, set()).add(unit)
+            worst = max(worst, max(len(v) for v in banks.values()))
+    return worst
+
+
+def cpb(T):   # fufft_internal.cuh cpb_for()
+    return 1 if T >= 256 else 256 // T
+
+
+@pytest.mark.parametrize("R,sizes", [(16, [16, 32, 64, 128, 256, 512, 1024, 2048, 4096, 8192]),
+                                     (8, [8, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096])])
+def test_exchanges_conflict_free(R, sizes):
+    for n in sizes:
+        T = n // R
+        nthr = cpb(T) * T
+        for p, (r, M) in enumerate(passes(n, R)):
+            width = 16 if M == 1 else 8
+            addrs = []
+            for tid in range(nthr):
+                slot, lane = divmod(tid, T)
+                pos = positions(n, R, p, lane)
+                if width == 16:
+                    assert all(q % 2 == 0 for q in pos[::2])
+                    addrs.append([swz(slot * n + q) for q in pos[::2]])
+                else:
+                    addrs.append([swz(slot * n + q) for q in pos])
+            assert worst_ways(addrs, width) == 1, (R, n, p, r, M)
+
+
+def test_swizzle_bijective_and_pair_preserving():
+    for k in range(4, 17):
+        img = [swz(p) for p in range(1 << k)]
+        assert len(set(img)) == 1 << k
+        assert all(swz(p) ^ p < 16 and (swz(p) & 1) == (p & 1) for p in range(1 << k))
