@@ -10,7 +10,8 @@ import ctypes as ct
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libfufft_b200.so")
+# FUFFT_B200_LIB points at another build of the same library (A/B runs)
+LIB_PATH = os.environ.get("FUFFT_B200_LIB") or os.path.join(HERE, "libfufft_b200.so")
 
 # enums of include/fufft_b200.h
 OK = 0

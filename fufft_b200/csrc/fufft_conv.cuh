@@ -94,6 +94,7 @@ __device__ __forceinline__ void visit(int lane, F&& f)
 }
 
 // DIF (S = -1): butterfly, then W^{jk}.  DIT (S = +1): conj(W^{jk}), then butterfly.
+// One table load (W_{rM}^j) per group; the powers are formed in registers.
 template<class C, int p, int S>
 __device__ __forceinline__ void butterflies(float2 (&x)[C::R], int lane, const float2* __restrict__ twt)
 {
@@ -102,15 +103,17 @@ __device__ __forceinline__ void butterflies(float2 (&x)[C::R], int lane, const f
    for(int s = 0; s < G; ++s) {
       float2* u = x + s * r;
       if constexpr(M > 1) {
-         const float2* tw = twt + tw_offset(r, M) + ((lane + s * T) & (M - 1));
+         const float2 w1 = __ldca(twt + tw_offset(r * M) + ((lane + s * T) & (M - 1)));
+         float2 w[r];
+         twiddle_powers<r>(w1, w);
          if constexpr(S > 0) {
 #pragma unroll
-            for(int k = 1; k < r; ++k) u[k] = cmulc(u[k], __ldca(tw + k * M));
+            for(int k = 1; k < r; ++k) u[k] = cmulc(u[k], w[k]);
          }
          dft<r, S>(u);
          if constexpr(S < 0) {
 #pragma unroll
-            for(int k = 1; k < r; ++k) u[k] = cmul(u[k], __ldca(tw + k * M));
+            for(int k = 1; k < r; ++k) u[k] = cmul(u[k], w[k]);
          }
       } else {
          dft<r, S>(u);
@@ -118,33 +121,42 @@ __device__ __forceinline__ void butterflies(float2 (&x)[C::R], int lane, const f
    }
 }
 
+// Swizzle policies of the exchange buffer (float2 index -> float2 slot).
+//   SwzEngine: swz() above, 1-way for every size of both engines.
+//   Swz128:    exactly the TMA SWIZZLE_128B pattern (16-byte chunk bits 4..6
+//              of the byte address XOR bits 7..9), so a buffer filled by a
+//              swizzled TMA tensor load is already in exchange order; 1-way
+//              for every pattern with n >= 256 (radix 16) / n >= 8 (radix 8).
+struct SwzEngine { __device__ __forceinline__ static int map(int p) { return swz(p); } };
+struct Swz128 { __device__ __forceinline__ static int map(int p) { return p ^ (((p >> 4) & 7) << 1); } };
+
 // exchange through the swizzled shared buffer; `off` = slot * N
-template<class C, int p>
+template<class C, int p, class SW = SwzEngine>
 __device__ __forceinline__ void xstore(float2* X, int off, const float2 (&x)[C::R], int lane)
 {
    if constexpr(C::stride(p) == 1) {
       const int base = off + lane * C::R;
 #pragma unroll
       for(int k = 0; k < C::R; k += 2)
-         *reinterpret_cast<float4*>(X + swz(base + k)) = make_float4(x[k].x, x[k].y, x[k + 1].x, x[k + 1].y);
+         *reinterpret_cast<float4*>(X + SW::map(base + k)) = make_float4(x[k].x, x[k].y, x[k + 1].x, x[k + 1].y);
    } else {
-      visit<C, p>(lane, [&](int i, int pos) { X[swz(off + pos)] = x[i]; });
+      visit<C, p>(lane, [&](int i, int pos) { X[SW::map(off + pos)] = x[i]; });
    }
 }
 
-template<class C, int p>
+template<class C, int p, class SW = SwzEngine>
 __device__ __forceinline__ void xload(const float2* X, int off, float2 (&x)[C::R], int lane)
 {
    if constexpr(C::stride(p) == 1) {
       const int base = off + lane * C::R;
 #pragma unroll
       for(int k = 0; k < C::R; k += 2) {
-         const float4 v = *reinterpret_cast<const float4*>(X + swz(base + k));
+         const float4 v = *reinterpret_cast<const float4*>(X + SW::map(base + k));
          x[k] = make_float2(v.x, v.y);
          x[k + 1] = make_float2(v.z, v.w);
       }
    } else {
-      visit<C, p>(lane, [&](int i, int pos) { x[i] = X[swz(off + pos)]; });
+      visit<C, p>(lane, [&](int i, int pos) { x[i] = X[SW::map(off + pos)]; });
    }
 }
 

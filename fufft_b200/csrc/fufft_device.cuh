@@ -11,6 +11,7 @@
 //     W_{rM}^{jk}; the DIT pass multiplies by the conjugate first, then runs
 //     the inverse DFT_r (fufft.cuh:460-502, :723-750).
 #pragma once
+#include <cuda.h>   // CUtensorMap
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -133,21 +134,37 @@ template<int R, int S> __device__ __forceinline__ void dft(float2* x)
 }
 
 // ---------------------------------------------------------------------------
-// twiddle tables: for each radix r in {2,4,8,16} and stride M (r*M <= 2^16)
-// a table tw[k*M + j] = W_{rM}^{jk} = exp(-2 pi i jk / (rM)), k < r, j < M,
-// computed once per device in fp64 and rounded to fp32.  Transposed ([k][j])
-// so that the lanes of a warp, which hold consecutive j, read consecutive
-// addresses.
+// twiddle table: for every power of two L <= 2^16 the L values
+// W_L^j = exp(-2 pi i j / L), j < L, from fp64 sincospi rounded once to fp32
+// (tw_offset(L) = L - 2).  A radix-r pass at stride M needs W_{rM}^{jk}, k < r:
+// it loads the single value W_{rM}^j and forms the powers in registers
+// (twiddle_powers), so the whole table a transform touches is a few KB and
+// stays L1-resident.
 // ---------------------------------------------------------------------------
-constexpr int TW_LOG_MAX = 16;                       // largest r*M
-__host__ __device__ constexpr int tw_block(int r) { return (2 << TW_LOG_MAX) - r; }
-__host__ __device__ constexpr int tw_base(int r)
+constexpr int TW_LOG_MAX = 16;                       // largest L
+__host__ __device__ constexpr int tw_offset(int L) { return L - 2; }
+constexpr int TW_TOTAL = (2 << TW_LOG_MAX) - 2;
+
+// w[k] = w1^k for k = 1 .. r-1 by a product tree of depth <= 4 (rounding
+// error of the power grows with the depth, not with k)
+template<int r>
+__device__ __forceinline__ void twiddle_powers(float2 w1, float2* w)
 {
-   return r == 2 ? 0 : r == 4 ? tw_block(2) : r == 8 ? tw_block(2) + tw_block(4)
-                                            : tw_block(2) + tw_block(4) + tw_block(8);
+   w[1] = w1;
+   if constexpr(r > 2) w[2] = cmul(w1, w1);
+   if constexpr(r > 3) w[3] = cmul(w[2], w1);
+   if constexpr(r > 4) {
+      w[4] = cmul(w[2], w[2]);
+      w[5] = cmul(w[4], w1);
+      w[6] = cmul(w[4], w[2]);
+      w[7] = cmul(w[4], w[3]);
+   }
+   if constexpr(r > 8) {
+      w[8] = cmul(w[4], w[4]);
+#pragma unroll
+      for(int k = 9; k < 16; ++k) w[k] = cmul(w[8], w[k - 8]);
+   }
 }
-__host__ __device__ constexpr int tw_offset(int r, int M) { return tw_base(r) + r * (M - 1); }
-constexpr int TW_TOTAL = tw_base(16) + tw_block(16);
 
 // ---------------------------------------------------------------------------
 // shared-memory swizzle: XOR bits 1..3 of the float2 index with a function of
@@ -182,6 +199,26 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                 :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
+// 2-D tiled TMA load of box (x, y) of a tensor map into shared memory,
+// completion on `bar`.  No multicast: every CTA loads its own tiles.  x is
+// always 0 here (whole 128-byte rows), so the 16-byte rule on x holds.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar)
+{
+   asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                " [%0], [%1, {%2, %3}], [%4];"
+                :: "r"(smem_u32(dst)), "l"(tm), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tm)
+{
+   asm volatile("prefetch.tensormap [%0];" :: "l"(tm) : "memory");
+}
+// orders this thread's generic-proxy shared-memory accesses before later
+// async-proxy (TMA) writes to the same memory
+__device__ __forceinline__ void fence_proxy_async_smem()
+{
+   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
 {
    uint32_t ok;

@@ -10,6 +10,7 @@
 
 #include "../../include/fufft_b200.h"
 #include "fufft_conv.cuh"
+#include "fufft_stream.cuh"
 
 namespace fufft {
 namespace host {
@@ -66,6 +67,71 @@ fufft_status launch(const ConvArgs& args, cudaStream_t st, int device)
    return check(cudaGetLastError());
 }
 
+// ---- persistent TMA-pipelined kernel (fufft_stream.cuh) -------------------
+// 2-D tensor map over `bytes` of data seen as 128-byte rows (32 fp32 or 32
+// 32-bit words each), box = box_rows rows, SWIZZLE_128B
+fufft_status encode_rows_tmap(CUtensorMap* tm, const void* base, unsigned long long bytes, int box_rows, bool words);
+int sm_count(int device);
+
+template<int N, int R, bool BFP, Mid MID, bool FLIN>
+fufft_status launch_stream(const ConvArgs& args, cudaStream_t st, int device)
+{
+   constexpr int T = N / R;
+   constexpr int CPB = cpb_for(T);
+   using K = StreamKernel<N, R, CPB, BFP, MID, FLIN>;
+   auto kern = conv_stream_kernel<N, R, CPB, BFP, MID, FLIN>;
+   static std::atomic<uint64_t> configured{0};
+   static std::atomic<int> blocks_per_sm[64];
+   const uint64_t bit = 1ull << (device & 63);
+   if(!(configured.load(std::memory_order_acquire) & bit)) {
+      fufft_status s = check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)K::SMEM));
+      if(s != FUFFT_OK) return s;
+      // ask for the smallest shared-memory carveout that still holds the
+      // resident CTAs, so the rest of the 256 KB stays L1 for the twiddle tables
+      const int per_sm_kb = (int)(((K::THREADS <= 256 ? 2 : 1) * (K::SMEM + 1024) + 1023) / 1024);
+      const int pct = per_sm_kb >= 228 ? 100 : (per_sm_kb * 100 + 227) / 228;
+      s = check(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, pct));
+      if(s != FUFFT_OK) return s;
+      int nb = 0;
+      s = check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, K::THREADS, K::SMEM));
+      if(s != FUFFT_OK) return s;
+      blocks_per_sm[device & 63].store(nb > 0 ? nb : 1);
+      configured.fetch_or(bit, std::memory_order_acq_rel);
+   }
+   const long long ngroups = (args.batch + CPB - 1) / CPB;
+   CUtensorMap ta, tb;
+   fufft_status s = encode_rows_tmap(&ta, args.a, (unsigned long long)args.batch * N * K::EB, K::SIG_BOX, BFP);
+   if(s != FUFFT_OK) return s;
+   if constexpr(MID != Mid::NONE) {
+      const unsigned long long fbytes = ((unsigned long long)(args.batch - 1) * args.filter_stride + N) * K::EB;
+      s = encode_rows_tmap(&tb, args.b, fbytes, K::FLT_BOX, BFP);
+      if(s != FUFFT_OK) return s;
+   } else {
+      tb = ta;
+   }
+   const long long cap = (long long)sm_count(device) * blocks_per_sm[device & 63].load();
+   const long long grid = ngroups < cap ? ngroups : cap;
+   kern<<<(unsigned)grid, K::THREADS, K::SMEM, st>>>(ta, tb, args, ngroups);
+   count_launch();
+   return check(cudaGetLastError());
+}
+
+template<int R, bool BFP, Mid MID, bool FLIN>
+fufft_status launch_stream_n(int n, const ConvArgs& args, cudaStream_t st, int device)
+{
+#define FUFFT_SCASE(NN)                                                                \
+   case NN:                                                                            \
+      if constexpr(NN >= R && NN * (BFP ? 4 : 8) >= 128 && NN <= (R == 8 ? MAX_N_R8 : MAX_N_R16)) \
+         return launch_stream<NN, R, BFP, MID, FLIN>(args, st, device);                \
+      else return FUFFT_ERR_UNSUPPORTED;
+   switch(n) {
+      FUFFT_SCASE(16) FUFFT_SCASE(32) FUFFT_SCASE(64) FUFFT_SCASE(128) FUFFT_SCASE(256)
+      FUFFT_SCASE(512) FUFFT_SCASE(1024) FUFFT_SCASE(2048) FUFFT_SCASE(4096) FUFFT_SCASE(8192)
+   default: return FUFFT_ERR_UNSUPPORTED;
+   }
+#undef FUFFT_SCASE
+}
+
 // runtime n -> instantiation
 template<int R, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>
 fufft_status launch_n(int n, const ConvArgs& args, cudaStream_t st, int device)
@@ -103,6 +169,43 @@ fufft_status dispatch_mid(int n, fufft_midop mid, bool bperm, const ConvArgs& a,
                    : launch_n<R, IN, OUT, Mid::CONJ, Flt::GLOBAL, FBFP>(n, a, st, dev);
    }
    return FUFFT_ERR_INVALID_ARG;
+}
+
+// fp32 / BFP convolution.  Measured on B200 (N = 512..8192, 1 GiB signal):
+// the direct kernel (fufft_conv.cuh) is fastest whenever the filter arrives in
+// the register-boundary layout (TMA bulk prefetch) and for BFP; the
+// persistent TMA-pipelined kernel (fufft_stream.cuh) wins for an fp32 filter
+// in the linear chain order (it stages that filter through a swizzled TMA
+// tensor load instead of 128-byte-per-thread global reads).  The pipelined
+// kernel needs 16-byte aligned signal and filter and whole 128-byte rows per
+// transform and per filter stride; otherwise the direct kernel runs.
+template<int R, bool BFP>
+fufft_status dispatch_conv(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
+{
+   const int eb = BFP ? 4 : 8;
+#ifdef FUFFT_NO_STREAM
+   const bool ok = false;
+#else
+   const bool ok = !BFP && !bperm && mid != FUFFT_MID_NONE && n * eb >= 128 && aligned(a.a, 16) &&
+                   aligned(a.b, 16) && (a.filter_stride * eb) % 128 == 0;
+#endif
+   if(ok) {
+      fufft_status s = FUFFT_ERR_UNSUPPORTED;
+      switch(mid) {
+      case FUFFT_MID_NONE: s = launch_stream_n<R, BFP, Mid::NONE, false>(n, a, st, dev); break;
+      case FUFFT_MID_MULTIPLY:
+         s = bperm ? launch_stream_n<R, BFP, Mid::MUL, false>(n, a, st, dev)
+                   : launch_stream_n<R, BFP, Mid::MUL, true>(n, a, st, dev);
+         break;
+      case FUFFT_MID_CONJ_MULTIPLY:
+         s = bperm ? launch_stream_n<R, BFP, Mid::CONJ, false>(n, a, st, dev)
+                   : launch_stream_n<R, BFP, Mid::CONJ, true>(n, a, st, dev);
+         break;
+      }
+      if(s != FUFFT_ERR_UNSUPPORTED) return s;
+   }
+   return BFP ? dispatch_mid<R, In::BFP, Out::BFP, true>(n, mid, bperm, a, st, dev)
+              : dispatch_mid<R, In::C32, Out::C32, false>(n, mid, bperm, a, st, dev);
 }
 
 // one entry per kernel family and radix (each lives in its own translation

@@ -1,6 +1,7 @@
 // fufft_runtime.cu -- per-device state, index maps, filter preparation and
 // the int16 block-floating-point pack/unpack kernels of the C ABI.
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <atomic>
 #include <cmath>
@@ -16,24 +17,16 @@ namespace fufft {
 __device__ float2 g_twiddle[TW_TOTAL];
 __device__ unsigned int g_status;
 
-// fill every table: entry (r, M, k, j) = exp(-2 pi i jk / (rM)) from fp64
-// sincospi, rounded once to fp32
+// fill the table: entry L - 2 + j = exp(-2 pi i j / L) from fp64 sincospi,
+// rounded once to fp32
 __global__ void twiddle_init_kernel()
 {
    for(int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < TW_TOTAL; idx += gridDim.x * blockDim.x) {
-      int r = 16;
-      if(idx < tw_base(4)) r = 2;
-      else if(idx < tw_base(8)) r = 4;
-      else if(idx < tw_base(16)) r = 8;
-      const int off = idx - tw_base(r);
-      int M = 1;
-      while(r * (2 * M - 1) <= off) M *= 2;   // largest M with r*(M-1) <= off
-      const int e = off - r * (M - 1);         // k*M + j
-      const int k = e / M, j = e % M;
-      const long long L = (long long)r * M;
-      const long long jk = ((long long)j * k) % L;
+      int L = 2;
+      while(tw_offset(2 * L) <= idx) L *= 2;   // largest L with L - 2 <= idx
+      const int j = idx - tw_offset(L);
       double s, c;
-      sincospi(-2.0 * (double)jk / (double)L, &s, &c);
+      sincospi(-2.0 * (double)j / (double)L, &s, &c);
       g_twiddle[idx] = make_float2((float)c, (float)s);
    }
 }
@@ -74,6 +67,54 @@ fufft_status init_device(DevState& d)
    return s;
 }
 }  // namespace
+
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder()
+{
+   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+   static std::once_flag once;
+   std::call_once(once, [] {
+      void* p = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+         q == cudaDriverEntryPointSuccess)
+         fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+   });
+   return fn;
+}
+std::atomic<int> g_sms[MAX_DEVICES];
+}  // namespace
+
+fufft_status encode_rows_tmap(CUtensorMap* tm, const void* base, unsigned long long bytes, int box_rows, bool words)
+{
+   auto fn = tmap_encoder();
+   if(!fn) return FUFFT_ERR_UNSUPPORTED;
+   if(bytes % 128 || !aligned(base, 16) || box_rows < 1 || box_rows > 256) return FUFFT_ERR_MISALIGNED;
+   cuuint64_t dims[2] = {32, bytes / 128};
+   cuuint64_t strides[1] = {128};
+   cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
+   cuuint32_t estr[2] = {1, 1};
+   const CUresult r = fn(tm, words ? CU_TENSOR_MAP_DATA_TYPE_UINT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+   if(r != CUDA_SUCCESS) {
+      t_last_error = "cuTensorMapEncodeTiled failed";
+      return FUFFT_ERR_CUDA;
+   }
+   return FUFFT_OK;
+}
+
+int sm_count(int device)
+{
+   int v = g_sms[device & 63].load();
+   if(!v) {
+      cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device);
+      if(v <= 0) v = 1;
+      g_sms[device & 63].store(v);
+   }
+   return v;
+}
 
 fufft_status cuda_fail(cudaError_t e)
 {

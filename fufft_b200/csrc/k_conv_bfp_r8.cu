@@ -4,7 +4,7 @@ namespace fufft {
 namespace host {
 fufft_status family_conv_bfp_r8(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
 {
-   return dispatch_mid<8, In::BFP, Out::BFP, true>(n, mid, bperm, a, st, dev);
+   return dispatch_conv<8, true>(n, mid, bperm, a, st, dev);
 }
 }  // namespace host
 }  // namespace fufft

@@ -4,7 +4,7 @@ namespace fufft {
 namespace host {
 fufft_status family_conv_f32_r16(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
 {
-   return dispatch_mid<16, In::C32, Out::C32, false>(n, mid, bperm, a, st, dev);
+   return dispatch_conv<16, false>(n, mid, bperm, a, st, dev);
 }
 }  // namespace host
 }  // namespace fufft

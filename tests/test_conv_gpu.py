@@ -207,9 +207,10 @@ def test_errors_and_status(ops):
     a = torch.zeros(3 * 1000, dtype=torch.complex64, device="cuda")
     with pytest.raises(FufftError, match="INVALID_SIZE"):
         ops.conv(a, a, 1000, ops.LAYOUT_R16)
-    a = torch.zeros(4096, dtype=torch.complex64, device="cuda")
+    a = torch.zeros(8192, dtype=torch.complex64, device="cuda")
     with pytest.raises(FufftError, match="INVALID_SIZE"):
         ops.conv(a, a, 8192, ops.LAYOUT_R8)           # beyond the radix-8 one-kernel limit
+    a = torch.zeros(4096, dtype=torch.complex64, device="cuda")
     with pytest.raises(FufftError, match="MISALIGNED"):
         ops.conv(a, torch.view_as_complex(torch.view_as_real(a).view(-1)[2:-6].view(-1, 2)), 1024, ops.LAYOUT_R16)
     with pytest.raises(FufftError, match="INVALID_ARG"):
