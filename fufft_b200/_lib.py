@@ -34,6 +34,8 @@ SIGNATURES = {
     "fufft_filter_permute_host": (_I, [_P, _P, _I, _I, _I]),
     "fufft_filter_permute": (_I, [_P, _P, _I, _I, _I, _P]),
     "fufft_conv_c2c_f32": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I64, _P]),
+    "fufft_filter_permute2d": (_I, [_P, _P, _I, _I, _I, _I, _I, _P]),
+    "fufft_conv2d_f32": (_I, [_P, _P, _P, _I, _I, _I64, _I, _I, _I64, _P]),
     "fufft_fwd_f32": (_I, [_P, _P, _I, _I64, _I, _P]),
     "fufft_apply_f32": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I64, _I64, _P]),
     "fufft_conv_r2_f32": (_I, [_P, _P, _P, _P, _P, _I, _I64, _I, _I, _I64, _P]),

@@ -150,4 +150,31 @@ fufft_status fufft_conv_c2c_bfp(const int16_t* aq, const float* a_scale, const i
    return (R == 8 ? family_conv_bfp_r8 : family_conv_bfp_r16)(n, mid, layout_bperm(layout), args, st, dev);
 }
 
+fufft_status fufft_conv2d_f32(const float* a, const float* b, float* out, int h, int w, int64_t batch,
+                              fufft_layout layout, fufft_midop mid, int64_t filter_stride, fufft_stream_t stream)
+{
+   const int R = layout_radix(layout);
+   if(!R) return FUFFT_ERR_INVALID_ARG;
+   if(!pow2(h) || !pow2(w)) return FUFFT_ERR_INVALID_SIZE;
+   if(!(R == 8 ? conv2d_supported_r8(h, w) : conv2d_supported_r16(h, w))) return FUFFT_ERR_INVALID_SIZE;
+   if(batch < 0 || batch > (int64_t)1 << 40) return FUFFT_ERR_INVALID_BATCH;
+   if(batch == 0) return FUFFT_OK;
+   if(!a || !out) return FUFFT_ERR_INVALID_ARG;
+   if(!aligned(a, 8) || !aligned(out, 8)) return FUFFT_ERR_MISALIGNED;
+   fufft_status s = check_filter(b, mid, filter_stride, 8);
+   if(s != FUFFT_OK) return s;
+   DeviceCtx c;
+   if((s = device_ctx(&c)) != FUFFT_OK) return s;
+   ConvArgs args{};
+   args.tw = c.tw;
+   args.status = c.status;
+   args.batch = batch;
+   args.a = a;
+   args.b = b;
+   args.out = out;
+   args.filter_stride = filter_stride;
+   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+   return (R == 8 ? family_conv2d_r8 : family_conv2d_r16)(h, w, mid, layout_bperm(layout), args, st, c.device);
+}
+
 }  // extern "C"

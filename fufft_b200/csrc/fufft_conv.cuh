@@ -38,23 +38,47 @@ enum class Flt { NONE, SMEM, GLOBAL };     // filter read: TMA-staged register-b
 
 __host__ __device__ constexpr int ilog2c(long long n) { return n <= 1 ? 0 : 1 + ilog2c(n / 2); }
 
-template<int N_, int R_> struct Chain {
-   static constexpr int N = N_, R = R_;
-   static constexpr int LOGN = ilog2c(N), LOGR = ilog2c(R);
-   static constexpr int NR = LOGN / LOGR;
-   static constexpr int LEAD = 1 << (LOGN % LOGR);
-   static constexpr int NP = NR + (LEAD > 1 ? 1 : 0);
+// radix chain of one dimension of length n under base radix R:
+// [lead (if > 1), R, ..., R] with lead = 2^(log2 n mod log2 R)
+__host__ __device__ constexpr int dim_passes(int n, int R)
+{
+   return n <= 1 ? 0 : ilog2c(n) / ilog2c(R) + ((ilog2c(n) % ilog2c(R)) ? 1 : 0);
+}
+__host__ __device__ constexpr int dim_radix(int n, int R, int q)
+{
+   return ((ilog2c(n) % ilog2c(R)) && q == 0) ? (1 << (ilog2c(n) % ilog2c(R))) : R;
+}
+
+// Pass plan of an H x W transform (H = 1: a 1-D transform of W points).
+// Columns first: pass q of the H chain (radix r, per-column stride m) runs at
+// flattened stride M = W*m with twiddles W_{r m}^{j2 k}, j2 = row position
+// inside the group = (j >> log2 W) -- the column pass of fufft.cuh:1185-1207.
+// Then the W chain along rows (stride M < W, twiddles W_{r M}^{j k}), whose
+// last pass runs at M = 1 with radix R: the register boundary.  A 2-D DFT
+// has no twiddles between its dimensions, so the two chains commute and the
+// spectrum slot (r, c) holds frequency (rev_H(r), rev_W(c)).
+template<int H_, int W_, int R_> struct Chain2 {
+   static constexpr int H = H_, W = W_, R = R_, N = H_ * W_;
    static constexpr int T = N / R;
-   __host__ __device__ static constexpr int radix(int p) { return (LEAD > 1 && p == 0) ? LEAD : R; }
-   __host__ __device__ static constexpr int stride(int p)
+   static constexpr int NPC = dim_passes(H, R), NPR = dim_passes(W, R), NP = NPC + NPR;
+   __host__ __device__ static constexpr int radix(int p)
    {
-      int M = N;
-      for(int q = 0; q <= p; ++q) M /= radix(q);
-      return M;
+      return p < NPC ? dim_radix(H, R, p) : dim_radix(W, R, p - NPC);
    }
-   static_assert((1 << LOGN) == N && (1 << LOGR) == R, "powers of two only");
-   static_assert(NR >= 1, "the transform must hold at least one full radix-R pass");
+   __host__ __device__ static constexpr int dim_stride(int p)   // stride inside its own dimension
+   {
+      int m = p < NPC ? H : W;
+      for(int q = (p < NPC ? 0 : NPC); q <= p; ++q) m /= radix(q);
+      return m;
+   }
+   __host__ __device__ static constexpr int stride(int p) { return p < NPC ? W * dim_stride(p) : dim_stride(p); }
+   __host__ __device__ static constexpr bool tw_on(int p) { return dim_stride(p) > 1; }
+   __host__ __device__ static constexpr int tw_L(int p) { return radix(p) * dim_stride(p); }
+   __host__ __device__ static constexpr int tw_shift(int p) { return p < NPC ? ilog2c(W) : 0; }
+   static_assert((1 << ilog2c(H)) == H && (1 << ilog2c(W)) == W && (1 << ilog2c(R)) == R, "powers of two only");
+   static_assert(W >= R, "the row chain must end in a full radix-R pass (the register boundary)");
 };
+template<int N, int R> using Chain = Chain2<1, N, R>;
 
 struct ConvArgs {
    const void* a;          // signal: float2 (C32), packed int16 pairs (BFP), float xr (REAL2), spectrum (SPEC)
@@ -102,8 +126,9 @@ __device__ __forceinline__ void butterflies(float2 (&x)[C::R], int lane, const f
 #pragma unroll
    for(int s = 0; s < G; ++s) {
       float2* u = x + s * r;
-      if constexpr(M > 1) {
-         const float2 w1 = __ldca(twt + tw_offset(r * M) + ((lane + s * T) & (M - 1)));
+      if constexpr(C::tw_on(p)) {
+         const int j = ((lane + s * T) & (M - 1)) >> C::tw_shift(p);
+         const float2 w1 = __ldca(twt + tw_offset(C::tw_L(p)) + j);
          float2 w[r];
          twiddle_powers<r>(w1, w);
          if constexpr(S > 0) {
@@ -188,9 +213,10 @@ __device__ __forceinline__ uint32_t bfp_quant(float2 v, float inv)
    return ((uint32_t)(uint16_t)qy << 16) | (uint16_t)qx;
 }
 
-template<int N, int R, int CPB, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>
+template<class C_, int CPB, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>
 struct ConvKernel {
-   using C = Chain<N, R>;
+   using C = C_;
+   static constexpr int N = C::N, R = C::R;
    static constexpr int T = C::T;
    static constexpr int THREADS = CPB * T;
    static constexpr bool HAS_FILTER = (MID != Mid::NONE) && (OUT != Out::SPEC);
@@ -415,11 +441,11 @@ template<int THREADS> constexpr int min_blocks()
    return THREADS >= FUFFT_RESIDENT_THREADS ? 1 : FUFFT_RESIDENT_THREADS / THREADS;
 }
 
-template<int N, int R, int CPB, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>
-__global__ void __launch_bounds__(CPB * (N / R), min_blocks<CPB * (N / R)>())
+template<class C, int CPB, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>
+__global__ void __launch_bounds__(CPB * C::T, min_blocks<CPB * C::T>())
 conv_kernel(const ConvArgs args)
 {
-   ConvKernel<N, R, CPB, IN, OUT, MID, FLT, FBFP>::run(args);
+   ConvKernel<C, CPB, IN, OUT, MID, FLT, FBFP>::run(args);
 }
 
 }  // namespace fufft

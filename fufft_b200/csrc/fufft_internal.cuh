@@ -47,13 +47,12 @@ inline int max_n(int radix) { return radix == 8 ? MAX_N_R8 : radix == 16 ? MAX_N
 // transforms per CTA: about 256 threads per CTA, at least one full warp
 constexpr int cpb_for(int T) { return T >= 256 ? 1 : 256 / T; }
 
-template<int N, int R, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>
-fufft_status launch(const ConvArgs& args, cudaStream_t st, int device)
+template<class C, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>
+fufft_status launch_chain(const ConvArgs& args, cudaStream_t st, int device)
 {
-   constexpr int T = N / R;
-   constexpr int CPB = cpb_for(T);
-   using K = ConvKernel<N, R, CPB, IN, OUT, MID, FLT, FBFP>;
-   auto kern = conv_kernel<N, R, CPB, IN, OUT, MID, FLT, FBFP>;
+   constexpr int CPB = cpb_for(C::T);
+   using K = ConvKernel<C, CPB, IN, OUT, MID, FLT, FBFP>;
+   auto kern = conv_kernel<C, CPB, IN, OUT, MID, FLT, FBFP>;
    static std::atomic<uint64_t> configured{0};
    const uint64_t bit = 1ull << (device & 63);
    if(!(configured.load(std::memory_order_acquire) & bit)) {
@@ -130,6 +129,12 @@ fufft_status launch_stream_n(int n, const ConvArgs& args, cudaStream_t st, int d
    default: return FUFFT_ERR_UNSUPPORTED;
    }
 #undef FUFFT_SCASE
+}
+
+template<int N, int R, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>
+fufft_status launch(const ConvArgs& args, cudaStream_t st, int device)
+{
+   return launch_chain<Chain<N, R>, IN, OUT, MID, FLT, FBFP>(args, st, device);
 }
 
 // runtime n -> instantiation
@@ -221,6 +226,10 @@ fufft_status family_apply_r8(int, fufft_midop, bool, const ConvArgs&, cudaStream
 fufft_status family_apply_r16(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
 fufft_status family_r2_r8(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
 fufft_status family_r2_r16(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
+fufft_status family_conv2d_r8(int h, int w, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
+fufft_status family_conv2d_r16(int h, int w, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
+bool conv2d_supported_r8(int h, int w);
+bool conv2d_supported_r16(int h, int w);
 
 }  // namespace host
 }  // namespace fufft

@@ -160,42 +160,59 @@ __host__ __device__ inline long long chain_rev_dev(long long idx, const int* w, 
 }
 
 struct PermPlan {
-   int w[32];
+   int w[32];          // row-dimension (W) chain: bit-group widths in pass order
    int p = 0, m = 0;
+   int wh[32];         // column-dimension (H) chain; ph = 0 for 1-D
+   int ph = 0, mh = 0;
    int v = 1;          // register-boundary width (1 = plain chain order)
    int T = 1;
 };
 
-static fufft_status make_perm_plan(int n, fufft_layout layout, PermPlan* pl)
+static fufft_status dim_plan(int n, int R, int* w, int* p, int* m)
 {
-   const int R = host::layout_radix(layout);
-   if(!R) return FUFFT_ERR_INVALID_ARG;
    int rad[32];
-   const int nrad = fufft_chain(n, R, rad);
+   const int nrad = n > 1 ? fufft_chain(n, R, rad) : 0;
    if(nrad < 0) return FUFFT_ERR_INVALID_SIZE;
-   pl->p = nrad;
-   pl->m = 0;
+   *p = nrad;
+   *m = 0;
    for(int k = 0; k < nrad; k++) {
       int lw = 0;
       while((1 << lw) < rad[k]) lw++;
-      pl->w[k] = lw;
-      pl->m += lw;
+      w[k] = lw;
+      *m += lw;
    }
-   pl->v = host::layout_bperm(layout) ? R : 1;
-   pl->T = n / pl->v;
    return FUFFT_OK;
 }
 
-// destination position i -> natural spectrum index
+static fufft_status make_perm_plan2(int h, int wd, fufft_layout layout, PermPlan* pl)
+{
+   const int R = host::layout_radix(layout);
+   if(!R) return FUFFT_ERR_INVALID_ARG;
+   fufft_status s = dim_plan(wd, R, pl->w, &pl->p, &pl->m);
+   if(s != FUFFT_OK) return s;
+   s = dim_plan(h, R, pl->wh, &pl->ph, &pl->mh);
+   if(s != FUFFT_OK) return s;
+   pl->v = host::layout_bperm(layout) ? R : 1;
+   pl->T = h * wd / pl->v;
+   return FUFFT_OK;
+}
+
+static fufft_status make_perm_plan(int n, fufft_layout layout, PermPlan* pl)
+{
+   return make_perm_plan2(1, n, layout, pl);
+}
+
+// destination position i -> natural spectrum index.  chain[r*W + c] =
+// spectrum[rev_H(r)*W + rev_W(c)]; bperm[L + k*T] = chain[v*L + k]
 __host__ __device__ inline long long perm_src(long long i, const PermPlan& pl)
 {
-   long long c = i;   // chain position
-   if(pl.v > 1) {     // bperm[L + k*T] = chain[v*L + k]
+   long long c = i;
+   if(pl.v > 1) {
       const long long L = i % pl.T, k = i / pl.T;
       c = pl.v * L + k;
    }
-   // chain[c] = spectrum[rev(c)]
-   return chain_rev_dev(c, pl.w, pl.p, pl.m);
+   const long long row = c >> pl.m, col = c & ((1LL << pl.m) - 1);
+   return (chain_rev_dev(row, pl.wh, pl.ph, pl.mh) << pl.m) | chain_rev_dev(col, pl.w, pl.p, pl.m);
 }
 
 __global__ void filter_permute_kernel(const float2* __restrict__ in, float2* __restrict__ out, int n,
@@ -366,6 +383,36 @@ fufft_status fufft_filter_permute(const float* spec_natural, float* out, int n, 
    fufft_status s = make_perm_plan(n, layout, &pl);
    if(s != FUFFT_OK) return s;
    if(pl.v > 1 && n % pl.v) return FUFFT_ERR_INVALID_SIZE;
+   if(batch == 0) return FUFFT_OK;
+   const long long total = (long long)n * batch;
+   const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+   filter_permute_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const float2*>(spec_natural), reinterpret_cast<float2*>(out), n, total, pl);
+   host::count_launch();
+   return host::check(cudaGetLastError());
+}
+
+fufft_status fufft_filter_permute2d(const float* spec_natural, float* out, int h, int w, int batch,
+                                    fufft_layout layout, int on_host, fufft_stream_t stream)
+{
+   if(!spec_natural || !out || spec_natural == out) return FUFFT_ERR_INVALID_ARG;
+   if(batch < 0) return FUFFT_ERR_INVALID_BATCH;
+   if(!host::pow2(h) || !host::pow2(w)) return FUFFT_ERR_INVALID_SIZE;
+   PermPlan pl;
+   fufft_status s = make_perm_plan2(h, w, layout, &pl);
+   if(s != FUFFT_OK) return s;
+   const int n = h * w;
+   if(pl.v > 1 && n % pl.v) return FUFFT_ERR_INVALID_SIZE;
+   if(on_host) {
+      const float2* in = reinterpret_cast<const float2*>(spec_natural);
+      float2* o = reinterpret_cast<float2*>(out);
+      for(long long i = 0; i < n; i++) {
+         const long long src = perm_src(i, pl);
+         for(long long t = 0; t < batch; t++) o[t * n + i] = in[t * n + src];
+      }
+      return FUFFT_OK;
+   }
+   if(!host::aligned(spec_natural, 8) || !host::aligned(out, 8)) return FUFFT_ERR_MISALIGNED;
    if(batch == 0) return FUFFT_OK;
    const long long total = (long long)n * batch;
    const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);

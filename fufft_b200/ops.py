@@ -30,7 +30,8 @@ from ._lib import (LAYOUT_NATURAL, LAYOUT_R8, LAYOUT_R8_BPERM, LAYOUT_R16, LAYOU
 __all__ = [
     "MID_NONE", "MID_MULTIPLY", "MID_CONJ_MULTIPLY",
     "LAYOUT_R8", "LAYOUT_R8_BPERM", "LAYOUT_R16", "LAYOUT_R16_BPERM", "LAYOUT_NATURAL",
-    "FufftError", "chain", "chain_rev", "filter_permute", "filter_permute_host", "conv", "fwd", "apply",
+    "FufftError", "chain", "chain_rev", "filter_permute", "filter_permute_host", "filter_permute2d", "conv",
+    "conv2d", "fwd", "apply",
     "conv_r2", "bfp_pack", "bfp_unpack", "conv_bfp", "pipeline_ip", "pipeline_fused", "pipeline_v16",
     "pipeline_v16f", "pipeline_r16", "pipeline_fwd", "pipeline_apply", "pipeline_v16_bfp", "init",
     "device_status", "launch_count", "max_n",
@@ -127,6 +128,28 @@ def conv(a: torch.Tensor, b: torch.Tensor | None, n: int, layout: int = LAYOUT_R
     fs = n if filter_stride is None else filter_stride
     check(lib().fufft_conv_c2c_f32(_ptr(a), _ptr(bt), _ptr(out), n, _batch(a, n), layout, mid, fs, _stream()),
           "fufft_conv_c2c_f32")
+    return out
+
+
+def filter_permute2d(spec_natural: torch.Tensor, h: int, w: int, layout: int) -> torch.Tensor:
+    """natural-order 2-D spectrum (device, row-major) -> 2-D kernel layout"""
+    s = _complex(spec_natural).contiguous()
+    out = torch.empty_like(s)
+    check(lib().fufft_filter_permute2d(_ptr(s), _ptr(out), h, w, _batch(s, h * w), layout, 0, _stream()),
+          "fufft_filter_permute2d")
+    return out
+
+
+def conv2d(a: torch.Tensor, b: torch.Tensor | None, h: int, w: int, layout: int = LAYOUT_R16_BPERM,
+           mid: int = MID_MULTIPLY, filter_stride: int | None = None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """fufft_conv2d<H, W, CPB>: fused 2-D cyclic convolution of row-major h x w images"""
+    a = _complex(a)
+    bt = None if b is None else _complex(b)
+    out = torch.empty_like(a) if out is None else _complex(out)
+    fs = h * w if filter_stride is None else filter_stride
+    check(lib().fufft_conv2d_f32(_ptr(a), _ptr(bt), _ptr(out), h, w, _batch(a, h * w), layout, mid, fs, _stream()),
+          "fufft_conv2d_f32")
     return out
 
 

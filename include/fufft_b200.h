@@ -113,6 +113,14 @@ fufft_status fufft_filter_permute_host(const float* spec_natural, float* out, in
 fufft_status fufft_filter_permute(const float* spec_natural, float* out, int n, int batch,
                                   fufft_layout layout, fufft_stream_t stream);
 
+/* 2-D: slot (r, c) of the chain order holds spectrum (rev_H(r), rev_W(c)),
+ * each dimension reversed over its own chain ([lead, R, ...]; radix 8 on
+ * power-of-8 sides reproduces the reference's rev8 map, verify_kernel.cpp:738-748);
+ * the BPERM layouts then apply the register-boundary order to the flattened
+ * index.  on_host != 0: host pointers, synchronous; else device, async. */
+fufft_status fufft_filter_permute2d(const float* spec_natural, float* out, int h, int w, int batch,
+                                    fufft_layout layout, int on_host, fufft_stream_t stream);
+
 /* ---- fused fp32 convolution ---------------------------------------------
  * out = IDFT(DFT(a) . mid(filter)) for each transform, one kernel launch,
  * three HBM streams (signal, filter, result).  a == out is allowed.
@@ -124,6 +132,17 @@ fufft_status fufft_filter_permute(const float* spec_natural, float* out, int n, 
 fufft_status fufft_conv_c2c_f32(const float* a, const float* b, float* out, int n, int64_t batch,
                                 fufft_layout layout, fufft_midop mid, int64_t filter_stride,
                                 fufft_stream_t stream);
+
+/* ---- fused 2-D convolution ----------------------------------------------
+ * Row-major h x w images: 2-D DFT (columns then rows), mid-op against the
+ * 2-D filter spectrum (fufft_filter_permute2d order), inverse, one kernel
+ * launch per batch.  Replaces fufft_conv2d<H, W, CPB> (fufft.cuh:1209-1258,
+ * H, W powers of 8, H*W <= 4096, layout R8).  Here h, w are powers of two
+ * with w >= 8 (R8) / 16 (R16) and h*w <= 4096 (R8) / 8192 (R16) per CTA;
+ * filter_stride 0 shares one filter across the batch. */
+fufft_status fufft_conv2d_f32(const float* a, const float* b, float* out, int h, int w, int64_t batch,
+                              fufft_layout layout, fufft_midop mid, int64_t filter_stride,
+                              fufft_stream_t stream);
 
 /* ---- split forward / apply (one signal, many filters) -------------------
  * fwd: natural-order signal -> chain-order spectrum (layout R8 or R16 picks

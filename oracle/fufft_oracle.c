@@ -355,7 +355,7 @@ int orc_conv_r2(int n, int radix, const float* xr, const float* yr, const cpx* b
                 float* ur, float* vr, int batch, long long filter_stride)
 {
    const size_t count = (size_t)n * batch;
-   cpx* A = (cpx*)malloc(count * sizeof(cpx));
+   cpx* A = (cpx*)calloc(count, sizeof(cpx));
    if(!A) return -2;
    for(size_t i = 0; i < count; i++) A[i] = mk(xr[i], yr[i]);
    int rc = orc_conv(n, radix, ORC_MID_MULTIPLY, A, b_dr, A, batch, filter_stride);
@@ -383,6 +383,56 @@ static void col_pass(cpx* A, int H, int W, int m, int sign, int dit)
       if(!dit && m > 1) tw_chain(8, v, step, j2);
       for(int k = 0; k < 8; k++) A[base + k * W * m] = v[k];
    }
+}
+
+/* column pass of any radix r (<= 16): the reference's column pass
+ * (verify_kernel.cpp:681-698) with the radix generalised: taps at stride W*m,
+ * twiddle W_{r m}^{j2 k} by the running chain of apply_twiddles_r */
+static void col_pass_r(cpx* A, int H, int W, int m, int r, int sign, int dit)
+{
+   const float step = (float)sign * ORC_2PI_F / (float)(r * m);
+   const int G = H * W / r;
+   for(int g = 0; g < G; g++) {
+      const int c = g % W, g2 = g / W, j2 = g2 % m, b2 = g2 / m;
+      const int base = c + W * (b2 * r * m + j2);
+      cpx u[16], v[16];
+      for(int k = 0; k < r; k++) u[k] = A[base + k * W * m];
+      if(dit && m > 1) tw_chain(r, u, step, j2);
+      dftR(r, u, v, sign);
+      if(!dit && m > 1) tw_chain(r, v, step, j2);
+      for(int k = 0; k < r; k++) A[base + k * W * m] = v[k];
+   }
+}
+
+/* 2-D fused conv over the radix chains [lead, R, ...] of each side, in the
+ * reference's order (rows DIF, columns DIF, pointwise, columns DIT, rows
+ * DIT; verify_kernel.cpp:700-722).  For radix 8 on power-of-8 sides this is
+ * exactly kernel_conv2d; other chains are this library's extension of it.
+ * Filter slot (r, c) holds spectrum (rev_H(r), rev_W(c)). */
+int orc_conv2d(int H, int W, int radix, int mid, const cpx* a, const cpx* b2d, cpx* out, int batch,
+               long long filter_stride)
+{
+   int rh[32], rw[32];
+   const int nh = H > 1 ? chain_of(H, radix, rh) : 0;
+   const int nw = chain_of(W, radix, rw);
+   if(nh < 0 || nw < 0) return -1;
+   const int NP = H * W;
+   for(int t = 0; t < batch; t++) {
+      cpx* A = out + (size_t)t * NP;
+      const cpx* b = b2d + (size_t)((long long)t * filter_stride);
+      if(out != a) memcpy(A, a + (size_t)t * NP, (size_t)NP * sizeof(cpx));
+      int M = W;
+      for(int q = 0; q < nw; q++) { M /= rw[q]; pass_inplace(A, NP / rw[q], rw[q], M, -1, 0, 0); }
+      int m = H;
+      for(int q = 0; q < nh; q++) { m /= rh[q]; col_pass_r(A, H, W, m, rh[q], -1, 0); }
+      for(int i = 0; i < NP; i++) {
+         if(mid == ORC_MID_MULTIPLY) A[i] = cmul(A[i], b[i]);
+         else if(mid == ORC_MID_CONJ) A[i] = cmul_conj(A[i], b[i]);
+      }
+      for(int q = nh - 1; q >= 0; q--) { col_pass_r(A, H, W, m, rh[q], +1, 1); m *= rh[q]; }
+      for(int q = nw - 1; q >= 0; q--) { pass_inplace(A, NP / rw[q], rw[q], M, +1, 1, 0); M *= rw[q]; }
+   }
+   return 0;
 }
 
 /* fused 2-D conv for H, W powers of 8 (H*W <= 4096 in the reference):

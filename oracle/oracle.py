@@ -66,6 +66,7 @@ class Oracle:
             "orc_apply": (i, [i, i, i, _P, _P, _P, i, ll]),
             "orc_conv_r2": (i, [i, i, _P, _P, _P, _P, _P, i, ll]),
             "orc_conv2d_pow8": (i, [i, i, _P, _P, _P, i, ll]),
+            "orc_conv2d": (i, [i, i, i, i, _P, _P, _P, i, ll]),
             "orc_bfp_quantize_batch": (None, [_P, i, i, _P, _P]),
             "orc_bfp_dequantize_batch": (None, [_P, _P, i, i, _P]),
             "orc_conv_bfp": (i, [i, i, i, _P, _P, _P, _P, _P, _P, i, ll]),
@@ -153,6 +154,21 @@ class Oracle:
         fs = h * w if filter_stride is None else filter_stride
         assert self.L.orc_conv2d_pow8(h, w, _ptr(a), _ptr(b2d), _ptr(out), a.size // (h * w), fs) == 0
         return out
+
+    def conv2d(self, a, b2d, h: int, w: int, radix: int = 8, mid: int = MID_MULTIPLY,
+               filter_stride: int | None = None) -> np.ndarray:
+        a, b2d = _c64(a), _c64(b2d)
+        out = np.empty_like(a)
+        fs = h * w if filter_stride is None else filter_stride
+        assert self.L.orc_conv2d(h, w, radix, mid, _ptr(a), _ptr(b2d), _ptr(out), a.size // (h * w), fs) == 0
+        return out
+
+    def permute2d(self, b, h: int, w: int, radix: int) -> np.ndarray:
+        """natural 2-D spectrum -> chain order: slot (r, c) = spectrum(rev_H(r), rev_W(c))"""
+        rows = self.rev_table(self.chain(h, radix), h) if h > 1 else np.zeros(1, np.int64)
+        cols = self.rev_table(self.chain(w, radix), w)
+        bb = _c64(b).reshape(-1, h, w)
+        return np.ascontiguousarray(bb[:, rows][:, :, cols]).ravel()
 
     def bfp_quantize(self, x, n: int):
         x = _c64(x)
