@@ -42,6 +42,10 @@ SIGNATURES = {
     "fufft_bfp_pack": (_I, [_P, _P, _P, _I, _I64, _P]),
     "fufft_bfp_unpack": (_I, [_P, _P, _P, _I, _I64, _P]),
     "fufft_conv_c2c_bfp": (_I, [_P, _P, _P, _P, _P, _P, _I, _I64, _I, _I, _I64, _P]),
+    "fufft_large_plan": (_I, [_I64, _I, ct.POINTER(_I), ct.POINTER(_I)]),
+    "fufft_conv_large_f32": (_I, [_P, _P, _I64, _I64, _I, _I, _I, _I, _P]),
+    "fufft_conv_large_bfp_workspace": (ct.c_size_t, [_I64, _I64]),
+    "fufft_conv_large_bfp": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _I, _P, ct.c_size_t, _P]),
 }
 
 

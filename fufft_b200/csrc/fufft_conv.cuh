@@ -91,6 +91,7 @@ struct ConvArgs {
    float* out_scale;       // BFP: one scale per transform
    long long filter_stride;  // elements between consecutive transforms' filters; 0 = one shared filter
    long long spec_stride;    // SPEC input: elements between consecutive transforms' spectra
+   long long scale_div;      // BFP filter scale of transform t: b_scale[t / scale_div] (0, 1: per transform)
    long long batch;
    const float2* tw;         // the device's twiddle tables (tw_offset layout)
    unsigned int* status;     // device status word (bounded-wait reports)
@@ -347,7 +348,7 @@ struct ConvKernel {
                mbar_wait(&fbar, 0, args.status);
                if constexpr(FBFP) {
                   const uint32_t* Fs = reinterpret_cast<const uint32_t*>(F) + off;
-                  const float sb = active ? __ldg(args.b_scale + (args.filter_stride ? tr : 0)) : 0.0f;
+                  const float sb = active ? __ldg(args.b_scale + (args.filter_stride ? (args.scale_div > 1 ? tr / args.scale_div : tr) : 0)) : 0.0f;
 #pragma unroll
                   for(int k = 0; k < R; ++k) f[k] = bfp_dequant(Fs[lane + k * T], sb);
                } else {
@@ -358,7 +359,7 @@ struct ConvKernel {
             } else {
                const size_t fbase = (size_t)(tr * args.filter_stride) + (size_t)lane * R;
                if constexpr(FBFP) {
-                  const float sb = active ? __ldg(args.b_scale + (args.filter_stride ? tr : 0)) : 0.0f;
+                  const float sb = active ? __ldg(args.b_scale + (args.filter_stride ? (args.scale_div > 1 ? tr / args.scale_div : tr) : 0)) : 0.0f;
                   const uint4* fp = reinterpret_cast<const uint4*>(static_cast<const uint32_t*>(args.b) + fbase);
 #pragma unroll
                   for(int k = 0; k < R; k += 4) {

@@ -229,6 +229,11 @@ fufft_status family_r2_r16(int, fufft_midop, bool, const ConvArgs&, cudaStream_t
 fufft_status family_conv2d_r8(int h, int w, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
 fufft_status family_conv2d_r16(int h, int w, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
 bool conv2d_supported_r8(int h, int w);
+fufft_status family_mid_bfpfilter_r8(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
+fufft_status family_mid_bfpfilter_r16(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
+// fp32 -> int16 pairs with the per-transform abs-max already in `scale`
+// (fp32 bits); leaves scale = max(mx, 1e-30) / 32767
+fufft_status bfp_requantize(const float2* x, float* scale, uint32_t* q, long long n, long long batch, cudaStream_t st);
 bool conv2d_supported_r16(int h, int w);
 
 }  // namespace host

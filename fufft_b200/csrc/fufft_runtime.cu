@@ -251,7 +251,7 @@ __global__ void bfp_absmax_kernel(const float2* __restrict__ x, unsigned int* __
 }
 
 __global__ void bfp_quant_kernel(const float2* __restrict__ x, const float* __restrict__ mxv,
-                                 uint32_t* __restrict__ q, int n, long long total)
+                                 uint32_t* __restrict__ q, long long n, long long total)
 {
    for(long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x; g < total;
        g += (long long)gridDim.x * blockDim.x) {
@@ -274,6 +274,19 @@ __global__ void bfp_unpack_kernel(const uint32_t* __restrict__ q, const float* _
        g += (long long)gridDim.x * blockDim.x)
       x[g] = bfp_dequant(q[g], s[g / n]);
 }
+
+namespace host {
+fufft_status bfp_requantize(const float2* x, float* scale, uint32_t* q, long long n, long long batch, cudaStream_t st)
+{
+   const long long total = n * batch;
+   const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+   bfp_quant_kernel<<<blocks, 256, 0, st>>>(x, scale, q, n, total);
+   bfp_scale_kernel<<<(unsigned)((batch + 255) / 256), 256, 0, st>>>(scale, batch);
+   count_launch();
+   count_launch();
+   return check(cudaGetLastError());
+}
+}  // namespace host
 
 }  // namespace fufft
 

@@ -34,7 +34,7 @@ __all__ = [
     "conv2d", "fwd", "apply",
     "conv_r2", "bfp_pack", "bfp_unpack", "conv_bfp", "pipeline_ip", "pipeline_fused", "pipeline_v16",
     "pipeline_v16f", "pipeline_r16", "pipeline_fwd", "pipeline_apply", "pipeline_v16_bfp", "init",
-    "device_status", "launch_count", "max_n",
+    "device_status", "launch_count", "max_n", "large_plan", "conv_large", "conv_large_bfp",
 ]
 
 
@@ -183,6 +183,41 @@ def conv_r2(xr: torch.Tensor, yr: torch.Tensor, b: torch.Tensor, n: int, layout:
     check(lib().fufft_conv_r2_f32(_ptr(xr), _ptr(yr), _ptr(bt), _ptr(ur), _ptr(vr), n, _batch(xr, n),
                                   layout, mid, fs, _stream()), "fufft_conv_r2_f32")
     return ur, vr
+
+
+# ---- four-step large N ------------------------------------------------------------
+def large_plan(n: int, layout: int = LAYOUT_R16) -> tuple[int, int]:
+    r, m = ct.c_int(), ct.c_int()
+    check(lib().fufft_large_plan(n, layout, ct.byref(r), ct.byref(m)), "fufft_large_plan")
+    return r.value, m.value
+
+
+def conv_large(buf: torch.Tensor, b: torch.Tensor | None, n: int, layout: int = LAYOUT_R16,
+               mid: int = MID_MULTIPLY, r_out: int | None = None, mid_size: int | None = None) -> torch.Tensor:
+    """run_large: in-place four-step convolution of transforms of n points"""
+    buf = _complex(buf)
+    if r_out is None or mid_size is None:
+        r_out, mid_size = large_plan(n, layout)
+    bt = None if b is None else _complex(b)
+    check(lib().fufft_conv_large_f32(_ptr(buf), _ptr(bt), n, _batch(buf, n), r_out, mid_size, layout, mid,
+                                     _stream()), "fufft_conv_large_f32")
+    return buf
+
+
+def conv_large_bfp(aq, a_scale, bq, b_scale, n: int, layout: int = LAYOUT_R16, mid: int = MID_MULTIPLY,
+                   r_out: int | None = None, mid_size: int | None = None, workspace: torch.Tensor | None = None):
+    if r_out is None or mid_size is None:
+        r_out, mid_size = large_plan(n, layout)
+    batch = _batch(aq, n, 2)
+    need = int(lib().fufft_conv_large_bfp_workspace(n, batch))
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=aq.device)
+    oq = torch.empty_like(aq)
+    os_ = torch.empty(batch, dtype=torch.float32, device=aq.device)
+    check(lib().fufft_conv_large_bfp(_ptr(aq), _ptr(a_scale), _ptr(bq), _ptr(b_scale), _ptr(oq), _ptr(os_), n, batch,
+                                     r_out, mid_size, layout, mid, _ptr(workspace), workspace.numel(), _stream()),
+          "fufft_conv_large_bfp")
+    return oq, os_
 
 
 # ---- int16 block floating point -------------------------------------------------

@@ -184,6 +184,32 @@ fufft_status fufft_conv_c2c_bfp(const int16_t* aq, const float* a_scale, const i
                                 fufft_layout layout, fufft_midop mid, int64_t filter_stride,
                                 fufft_stream_t stream);
 
+/* ---- four-step large N -------------------------------------------------
+ * N = r_out^LOUT * mid (r_out 8 or 16, mid a one-kernel size >= 256 of the
+ * layout's radix): LOUT outer DIF passes over HBM, the fused convolution on
+ * each mid-point chunk, LOUT outer DIT passes (4*LOUT + 3 HBM passes).  The
+ * filter is in the chain order of the whole sequence [r_out]*LOUT ++ middle
+ * chain (verify_kernel.cpp:460-477 chain_rev; bench_fufft.cu:414-428); with a
+ * BPERM layout each mid-point chunk of it is additionally in the middle's
+ * register-boundary order.  fp32 runs in place on buf.
+ * Replaces run_large / fufft_outer_pass_r / MidLaunch (bench_fufft.cu:368-451,
+ * fufft.cuh:1113-1165, :1717-1734).
+ * fufft_large_plan picks (r_out, mid) for n: radix-16 outer levels first. */
+fufft_status fufft_large_plan(int64_t n, fufft_layout layout, int* r_out, int* mid);
+fufft_status fufft_conv_large_f32(float* buf, const float* b, int64_t n, int64_t batch, int r_out, int mid,
+                                  fufft_layout layout, fufft_midop mid_op, fufft_stream_t stream);
+/* int16-BFP four-step (new: the reference's four-step is fp32 only).  Input,
+ * filter and output are int16 pairs with one scale per N-point transform
+ * (filter: quantised as one N-point block in chain order).  The intermediate
+ * passes run in fp32 in a caller-provided workspace of
+ * fufft_conv_large_bfp_workspace(n, batch) bytes (16-byte aligned); the output
+ * scale is max|.|/32767 over the whole transform, as in the one-kernel form. */
+size_t fufft_conv_large_bfp_workspace(int64_t n, int64_t batch);
+fufft_status fufft_conv_large_bfp(const int16_t* aq, const float* a_scale, const int16_t* bq, const float* b_scale,
+                                  int16_t* oq, float* o_scale, int64_t n, int64_t batch, int r_out, int mid,
+                                  fufft_layout layout, fufft_midop mid_op, void* workspace, size_t workspace_bytes,
+                                  fufft_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,98 @@
+"""GPU parity of the four-step large-N convolution (fufft_conv_large_f32 /
+_bfp) against the oracle on the reference's own cases
+(verify_kernel.cpp:1455-1460 test_large_cfg, pinned bit-exact by
+tests/test_oracle_golden.py), plus full-size
+properties."""
+import numpy as np
+import pytest
+import torch
+
+from oracle.oracle import MID_NONE, rel_l2
+
+pytestmark = pytest.mark.gpu
+F32_TOL = 2e-6
+BFP_TOL = 6e-5
+
+
+@pytest.fixture(scope="module")
+def ops():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from fufft_b200 import ops as o
+    o.init()
+    return o
+
+
+def _dev(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def _chunk_bperm(x, mid, v):
+    T = mid // v
+    i = np.arange(mid)
+    src = v * (i % T) + i // T
+    return np.ascontiguousarray(x.reshape(-1, mid)[:, src].ravel())
+
+
+CASES = [(32768, 2, 8, 4096, False), (32768, 2, 8, 4096, True), (32768, 2, 16, 2048, True),
+         (131072, 1, 16, 8192, True), (524288, 1, 16, 2048, True)]
+
+
+@pytest.mark.parametrize("n,batch,r_out,mid,v16", CASES)
+def test_large_reference_cases(ops, oracle, n, batch, r_out, mid, v16):
+    mr = 16 if v16 else 8
+    a, b = oracle.gen_large_cfg(n, batch, r_out, mid)
+    rev = oracle.rev_table(oracle.foursteps_chain(n, r_out, mid, mr), n)
+    b_dr = np.ascontiguousarray(b.reshape(batch, n)[:, rev]).ravel()
+    want = oracle.conv_foursteps(a, b_dr, n, r_out, mid, mr)
+    lay, lay_b = (ops.LAYOUT_R16, ops.LAYOUT_R16_BPERM) if v16 else (ops.LAYOUT_R8, ops.LAYOUT_R8_BPERM)
+    got = ops.conv_large(_dev(a), _dev(b_dr), n, lay, r_out=r_out, mid_size=mid).cpu().numpy()
+    assert rel_l2(got, want) <= F32_TOL
+    assert rel_l2(got[:n], oracle.conv_f64(a[:n], b[:n], n)) < 5e-6   # verify_kernel.cpp:524
+    got = ops.conv_large(_dev(a), _dev(_chunk_bperm(b_dr, mid, mr)), n, lay_b, r_out=r_out, mid_size=mid)
+    assert rel_l2(got.cpu().numpy(), want) <= F32_TOL
+
+
+def test_large_plan_matches_reference_recipes(ops):
+    assert ops.large_plan(32768, ops.LAYOUT_R16) == (16, 2048)        # bench_fufft.cu:520
+    assert ops.large_plan(262144, ops.LAYOUT_R16) == (16, 1024)       # bench_fufft.cu:521
+    assert ops.large_plan(1 << 26, ops.LAYOUT_R16) == (16, 1024)
+
+
+@pytest.mark.parametrize("n,batch", [(32768, 3), (262144, 1)])
+def test_large_bfp(ops, oracle, n, batch):
+    r_out, mid = ops.large_plan(n, ops.LAYOUT_R16)
+    rng = np.random.default_rng(n)
+    a = (rng.standard_normal(n * batch) + 1j * rng.standard_normal(n * batch)).astype(np.complex64)
+    taps = (rng.uniform(-1, 1, n * batch) + 1j * rng.uniform(-1, 1, n * batch))
+    spec = (np.fft.fft(taps.reshape(batch, n), axis=1) / n).astype(np.complex64).ravel()
+    rev = oracle.rev_table(oracle.foursteps_chain(n, r_out, mid, 16), n)
+    b_dr = np.ascontiguousarray(spec.reshape(batch, n)[:, rev]).ravel()
+    aq, as_ = oracle.bfp_quantize(a, n)
+    bq, bs = oracle.bfp_quantize(b_dr, n)
+    # oracle: dequantise, fp32 four-step, requantise (the same steps the library runs)
+    want_f = oracle.conv_foursteps(oracle.bfp_dequantize(aq, as_, n), oracle.bfp_dequantize(bq, bs, n),
+                                   n, r_out, mid, 16)
+    wq, ws = oracle.bfp_quantize(want_f, n)
+    oq, os_ = ops.conv_large_bfp(_dev(aq), _dev(as_), _dev(bq), _dev(bs), n, ops.LAYOUT_R16)
+    got = oracle.bfp_dequantize(oq.cpu().numpy(), os_.cpu().numpy(), n)
+    assert rel_l2(got, oracle.bfp_dequantize(wq, ws, n)) <= BFP_TOL
+    # whole pipeline against the unquantised fp64 convolution
+    rel = rel_l2(got[:n], oracle.conv_f64(a[:n], spec[:n], n))
+    assert rel < 3e-4
+
+
+def test_large_full_size_properties(ops):
+    """config 5 (N=32768, batch 2048): identity filter and round trip, checked
+    on the whole batch (size-independent properties)"""
+    n, batch = 32768, 2048
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5032768)
+    a = torch.randn(n * batch, dtype=torch.complex64, device="cuda", generator=g)
+    ident = torch.full((n * batch,), 1.0 / n, dtype=torch.complex64, device="cuda")   # DFT of a delta / n
+    out = ops.conv_large(a.clone(), ident, n, ops.LAYOUT_R16)
+    assert float((out - a).abs().pow(2).sum() / a.abs().pow(2).sum()) ** 0.5 < 2e-6
+    rt = ops.conv_large(a.clone(), None, n, ops.LAYOUT_R16, MID_NONE)
+    assert float((rt / n - a).abs().pow(2).sum() / a.abs().pow(2).sum()) ** 0.5 < 2e-6
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
