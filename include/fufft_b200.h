@@ -210,6 +210,23 @@ fufft_status fufft_conv_large_bfp(const int16_t* aq, const float* a_scale, const
                                   fufft_layout layout, fufft_midop mid_op, void* workspace, size_t workspace_bytes,
                                   fufft_stream_t stream);
 
+/* The same BFP four-step for callers that cannot allocate device memory when
+ * they call the library (a host whose device memory is entirely held by its
+ * own pool allocator, or a latency-critical loop where an allocation's
+ * possible device-wide synchronisation is not acceptable).  No counterpart in
+ * the reference.  Instead of a caller workspace it uses a fixed scratch area
+ * of FUFFT_NOALLOC_SCRATCH_BYTES that the library reserves on every GPU that
+ * loads it (held until exit): 8 * n * batch must not exceed it, else
+ * FUFFT_ERR_INVALID_SIZE.  All calls on a device share that area, so calls
+ * that may overlap on the GPU race -- keep them on one stream.  The first call
+ * on a device looks up the area's address; make it before any stream capture.
+ * Allocates nothing. */
+#define FUFFT_NOALLOC_SCRATCH_BYTES (16u << 20)
+fufft_status fufft_conv_large_bfp_noalloc(const int16_t* aq, const float* a_scale, const int16_t* bq,
+                                          const float* b_scale, int16_t* oq, float* o_scale, int64_t n,
+                                          int64_t batch, int r_out, int mid, fufft_layout layout,
+                                          fufft_midop mid_op, fufft_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
