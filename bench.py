@@ -268,6 +268,55 @@ def run_ours(args, rank, world, dist):
     return line
 
 
+def run_ncu_case():
+    """one launch of each headline kernel on a half-size batch (512 MiB signal,
+    still > L2), for ncu: fp32 (register-boundary filter), fp32 (linear chain
+    filter), int16-BFP (linear chain filter)"""
+    import torch
+    from fufft_b200 import ops
+    ops.init()
+    n, batch = N, POINTS // N // 2
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    a = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g)
+    b = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g) / n
+    out = torch.empty_like(a)
+    aq = torch.randint(-32767, 32767, (batch * n, 2), dtype=torch.int16, device="cuda", generator=g)
+    bq = torch.randint(-32767, 32767, (batch * n, 2), dtype=torch.int16, device="cuda", generator=g)
+    sc = torch.full((batch,), 1e-4, device="cuda")
+    ops.conv(a, b, n, ops.LAYOUT_R16_BPERM, ops.MID_MULTIPLY, out=out)
+    ops.conv(a, b, n, ops.LAYOUT_R16, ops.MID_MULTIPLY, out=out)
+    ops.conv_bfp(aq, sc, bq, sc, n, ops.LAYOUT_R16)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+
+
+def run_dist(args, rank, world, dist):
+    """one 2^26-point signal over `world` GPUs (config 5), two all-to-alls"""
+    import torch
+    from fufft_b200 import ops
+    from fufft_b200.distributed import GpuBackend, conv_distributed
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    ops.init()
+    n = 1 << 26
+    be = GpuBackend()
+    plan = be.plan(n, world)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5000 + rank)
+    x0 = torch.randn(world * plan.cols, dtype=torch.complex64, device=dev, generator=g)
+    bb = torch.randn(plan.n_blk, dtype=torch.complex64, device=dev, generator=g) / n
+    x = x0.clone()
+    ms = time_steps(torch, lambda: conv_distributed(x, bb, n, backend=be, plan=plan), args.steps, args.warmup, dist)
+    hbm, _ = peaks()
+    return {"metric": "distributed single-signal fused conv Gpoints/s, N=2^26", "value": round(n / (ms * 1e-3) / 1e9, 3),
+            "unit": "Gpoints/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "config": {"workload": "configs[4] single N=2^26 signal",
+            "plan": {"block": plan.n_blk, "r_out": plan.r_out, "mid": plan.mid, "chain": plan.chain},
+            "nvlink_bytes_per_gpu": 2 * 8 * plan.n_blk * (world - 1) // world}}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return None
@@ -301,7 +350,13 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=2.0, help="per-thread CPU baseline sample")
     ap.add_argument("--ref-seconds", type=float, default=1.0, help="per-thread sample per reference step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu-case", action="store_true", help="one launch per headline kernel, for ncu")
+    ap.add_argument("--workload", choices=["batch", "dist"], default="batch",
+                    help="dist: one 2^26-point signal over all ranks (2, 4 or 8)")
     args = ap.parse_args()
+    if args.ncu_case:
+        run_ncu_case()
+        return
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -315,7 +370,12 @@ def main():
         td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
         dist = td
     try:
-        line = run_reference(args, rank, world) if args.impl == "reference" else run_ours(args, rank, world, dist)
+        if args.impl == "reference":
+            line = run_reference(args, rank, world)
+        elif args.workload == "dist":
+            line = run_dist(args, rank, world, dist)
+        else:
+            line = run_ours(args, rank, world, dist)
         if rank == 0 and line is not None:
             print(json.dumps(line), flush=True)
     finally:

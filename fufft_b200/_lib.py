@@ -47,6 +47,7 @@ SIGNATURES = {
     "fufft_conv_large_bfp_workspace": (ct.c_size_t, [_I64, _I64]),
     "fufft_conv_large_bfp": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _I, _P, ct.c_size_t, _P]),
     "fufft_conv_large_bfp_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _I, _P]),
+    "fufft_dist_pass": (_I, [_P, _I, _I64, _I64, _I64, _I, _P]),
 }
 
 

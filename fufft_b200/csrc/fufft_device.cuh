@@ -200,7 +200,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                 :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 // 2-D tiled TMA load of box (x, y) of a tensor map into shared memory,
-// completion on `bar`.  No multicast: every CTA loads its own tiles.  x is
+// completion on `bar`.  Every CTA loads its own tiles from this GPU's memory.  x is
 // always 0 here (whole 128-byte rows), so the 16-byte rule on x holds.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar)
 {

@@ -210,6 +210,19 @@ fufft_status fufft_conv_large_bfp(const int16_t* aq, const float* a_scale, const
                                   fufft_layout layout, fufft_midop mid_op, void* workspace, size_t workspace_bytes,
                                   fufft_stream_t stream);
 
+/* ---- distributed single-signal convolution (new: the reference is single-GPU)
+ * One n-point transform over `world` ranks (2, 4 or 8), viewed as
+ * [world][n/world]: rank g holds columns col0 = g*cols .. col0+cols-1 of every
+ * row, cols = n/world^2, row k at x_local + k*cols.  fufft_dist_pass runs this
+ * rank's share of the first DIF (sign -1) or last DIT (sign +1) radix-world
+ * pass at stride n/world, in place.  Between the two, one all-to-all gives rank
+ * k block k, which is convolved as an n/world-point transform with block k of
+ * the chain-ordered filter (chain [world] ++ the block's chain); a second
+ * all-to-all returns it.  fufft_b200.distributed drives the sequence over
+ * torch.distributed (NCCL). */
+fufft_status fufft_dist_pass(float* x_local, int world, int64_t cols, int64_t col0, int64_t n, int sign,
+                             fufft_stream_t stream);
+
 /* The same BFP four-step for callers that cannot allocate device memory when
  * they call the library (a host whose device memory is entirely held by its
  * own pool allocator, or a latency-critical loop where an allocation's

@@ -582,6 +582,42 @@ int orc_conv_monolithic(long long n, int batch, int r_out, int mid, int mid_radi
    return 0;
 }
 
+/* ---- distributed single-signal convolution (host simulation) ------------- */
+
+/* one rank's share of the first (DIF) / last (DIT) radix-W pass of an n-point
+ * transform viewed as [W][n/W]: the rank holds columns col0 .. col0+cols-1 of
+ * every row, row k at A[k*cols ..].  Group = column j (global), taps = rows,
+ * twiddle W_n^{jk} (verify_kernel.cpp:319-337 flat pass, with the groups of one
+ * rank) */
+void orc_dist_pass(cpx* A, int W, long long cols, long long col0, long long n, int sign)
+{
+   const float step = (float)sign * ORC_2PI_F / (float)n;
+   for(long long jl = 0; jl < cols; jl++) {
+      const long long j = col0 + jl;
+      cpx u[16], v[16];
+      for(int k = 0; k < W; k++) u[k] = A[k * cols + jl];
+      if(sign > 0 && j) tw_chain(W, u, step, (int)j);
+      dftR(W, u, v, sign);
+      if(sign < 0 && j) tw_chain(W, v, step, (int)j);
+      for(int k = 0; k < W; k++) A[k * cols + jl] = v[k];
+   }
+}
+
+/* the whole distributed convolution on one host: radix-W DIF pass at stride
+ * n/W, then each n/W block through the one-kernel (mid == n/W) or four-step
+ * convolution with its slice of the chain-ordered filter, then the DIT pass */
+int orc_conv_dist(long long n, int W, int r_out, int mid, cpx* A, const cpx* b_dr)
+{
+   const long long blk = n / W;
+   pass_inplace(A, (size_t)blk, W, (int)blk, -1, 0, 0);
+   for(int k = 0; k < W; k++) {
+      if(blk == mid) orc_conv((int)blk, 16, ORC_MID_MULTIPLY, A + k * blk, b_dr + k * blk, A + k * blk, 1, blk);
+      else orc_conv_foursteps(blk, 1, r_out, mid, 16, A + k * blk, b_dr + k * blk);
+   }
+   pass_inplace(A, (size_t)blk, W, (int)blk, +1, 1, 0);
+   return 0;
+}
+
 /* ---- fp64 ground truth ----------------------------------------------------- */
 
 /* iterative radix-2 Cooley-Tukey in fp64: verify_kernel.cpp:434-456 */

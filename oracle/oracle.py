@@ -78,6 +78,8 @@ class Oracle:
             "orc_conv2d_f64": (None, [_P, _P, _P, i, i, i, ll]),
             "orc_ref_dft": (None, [_P, _P, i, i]),
             "orc_uniform_stream": (None, [ct.c_uint32, ll, _P]),
+            "orc_dist_pass": (None, [_P, i, ll, ll, ll, i]),
+            "orc_conv_dist": (i, [ll, i, i, i, _P, _P]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -255,6 +257,17 @@ class Oracle:
         s = self.uniform_stream(n * 77 + 5, 2 * n * batch + n)
         xy = s[: 2 * n * batch].reshape(-1, 2)
         return xy[:, 0].copy(), xy[:, 1].copy(), s[2 * n * batch:].copy()
+
+    # ---- distributed single-signal convolution ---------------------------
+    def dist_pass(self, x_local, W: int, cols: int, col0: int, n: int, sign: int) -> np.ndarray:
+        A = _c64(x_local).copy()
+        self.L.orc_dist_pass(_ptr(A), W, cols, col0, n, sign)
+        return A
+
+    def conv_dist(self, a, b_dr, n: int, W: int, r_out: int, mid: int) -> np.ndarray:
+        A = _c64(a).copy()
+        assert self.L.orc_conv_dist(n, W, r_out, mid, _ptr(A), _ptr(_c64(b_dr))) == 0
+        return A
 
     # ---- fp64 ground truth ------------------------------------------------
     def conv_f64(self, a, bnat, n: int, filter_stride: int | None = None) -> np.ndarray:
