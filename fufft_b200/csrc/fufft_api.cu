@@ -48,6 +48,26 @@ fufft_status fufft_conv_c2c_f32(const float* a, const float* b, float* out, int 
                                 fufft_layout layout, fufft_midop mid, int64_t filter_stride,
                                 fufft_stream_t stream)
 {
+   // radix-16 transforms beyond one CTA: the cluster-fused kernel (chain [C, 16, 16, 16])
+   if(layout_radix(layout) == 16 && pow2(n) && n > MAX_N_R16 && n <= MAX_N_CLUSTER) {
+      if(batch < 0 || batch > (int64_t)1 << 40) return FUFFT_ERR_INVALID_BATCH;
+      if(batch == 0) return FUFFT_OK;
+      if(!a || !out) return FUFFT_ERR_INVALID_ARG;
+      if(!aligned(a, 8) || !aligned(out, 8)) return FUFFT_ERR_MISALIGNED;
+      fufft_status s = check_filter(b, mid, filter_stride, 8);
+      if(s != FUFFT_OK) return s;
+      DeviceCtx c;
+      if((s = device_ctx(&c)) != FUFFT_OK) return s;
+      ConvArgs args{};
+      args.tw = c.tw;
+      args.status = c.status;
+      args.batch = batch;
+      args.a = a;
+      args.b = b;
+      args.out = out;
+      args.filter_stride = filter_stride;
+      return cluster_conv1d(n, mid, layout_bperm(layout), args, reinterpret_cast<cudaStream_t>(stream), c.device);
+   }
    ConvArgs args{};
    int R = 0, dev = 0;
    bool skip;
@@ -156,7 +176,8 @@ fufft_status fufft_conv2d_f32(const float* a, const float* b, float* out, int h,
    const int R = layout_radix(layout);
    if(!R) return FUFFT_ERR_INVALID_ARG;
    if(!pow2(h) || !pow2(w)) return FUFFT_ERR_INVALID_SIZE;
-   if(!(R == 8 ? conv2d_supported_r8(h, w) : conv2d_supported_r16(h, w))) return FUFFT_ERR_INVALID_SIZE;
+   const bool cluster = R == 16 && cluster_conv2d_shape(h, w);
+   if(!cluster && !(R == 8 ? conv2d_supported_r8(h, w) : conv2d_supported_r16(h, w))) return FUFFT_ERR_INVALID_SIZE;
    if(batch < 0 || batch > (int64_t)1 << 40) return FUFFT_ERR_INVALID_BATCH;
    if(batch == 0) return FUFFT_OK;
    if(!a || !out) return FUFFT_ERR_INVALID_ARG;
@@ -174,6 +195,7 @@ fufft_status fufft_conv2d_f32(const float* a, const float* b, float* out, int h,
    args.out = out;
    args.filter_stride = filter_stride;
    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+   if(cluster) return cluster_conv2d(h, w, mid, layout_bperm(layout), args, st, c.device);
    return (R == 8 ? family_conv2d_r8 : family_conv2d_r16)(h, w, mid, layout_bperm(layout), args, st, c.device);
 }
 

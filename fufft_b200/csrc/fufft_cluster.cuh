@@ -1,0 +1,247 @@
+// fufft_cluster.cuh -- fused convolution of transforms larger than one SM's
+// shared memory, in one kernel and three HBM passes, on a thread-block
+// cluster of C CTAs exchanging through distributed shared memory (DSMEM).
+//
+// The transform of NT = C * B points is seen as C rows of B points (row q =
+// positions q*B .. q*B + B-1).  Its radix chain starts with one pass of
+// radix C at stride B (the four-step's outer level), which mixes only the C
+// points of one column; the rest of the chain works inside rows.  So:
+//   1. CTA c loads columns c*B/C .. (c+1)*B/C - 1 of all rows straight from
+//      HBM (coalesced) and runs the radix-C DIF pass on them in registers;
+//   2. push: the value of row q goes into CTA q's shared buffer (st.shared::
+//      cluster), cluster barrier -- CTA q now holds row q;
+//   3. CTA q runs the fused one-CTA convolution on its B points (the engine of
+//      fufft_conv.cuh: DIF chain, filter block q at the register boundary,
+//      DIT chain), result back into its own buffer, cluster barrier;
+//   4. pull: CTA c reads its columns of every row from the other CTAs
+//      (ld.shared::cluster), cluster barrier (nobody exits while a peer still
+//      reads its memory), radix-C DIT pass in registers, coalesced stores.
+// The filter of the whole transform is in the chain order [C] ++ inner chain;
+// its block q is exactly the inner transform's own chain-ordered filter.
+// 1-D: N = 16384 (C 4), 32768 (C 8), 65536 (C 16) with B = 4096 and the
+// radix-16 chain [C, 16, 16, 16] -- the mixedrev16 order of N;
+// the four-step N = r_out * mid (the reference's N=32768 recipe: C = 16,
+// B = 2048, chain [16, 8, 16, 16]);
+// 2-D: the first column pass is the outer pass (per-column stride H/C,
+// twiddle index = row position inside the column group).
+// Cluster barriers are reached by every thread of every CTA on every path.
+#pragma once
+#include "fufft_conv.cuh"
+
+namespace fufft {
+
+__device__ __forceinline__ uint32_t cluster_ctarank()
+{
+   uint32_t r;
+   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+   return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x()
+{
+   uint32_t r;
+   asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+   return r;
+}
+__device__ __forceinline__ void cluster_sync()
+{
+   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cta address of this CTA -> the same offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_remote(uint32_t local_addr, uint32_t rank)
+{
+   uint32_t r;
+   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+   return r;
+}
+__device__ __forceinline__ void st_remote(uint32_t addr, float2 v)
+{
+   asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" :: "r"(addr), "f"(v.x), "f"(v.y) : "memory");
+}
+__device__ __forceinline__ float2 ld_remote(uint32_t addr)
+{
+   float2 v;
+   asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+   return v;
+}
+
+// Inner: the one-CTA chain of a row (Chain2); C: outer radix = CTAs per
+// cluster; OUT_L / OUT_SHIFT: the outer pass's twiddle W_{OUT_L}^{(col >> OUT_SHIFT) q}
+template<class Inner, int C, int OUT_L, int OUT_SHIFT, Mid MID, Flt FLT>
+struct ClusterConv {
+   using I = Inner;
+   static constexpr int B = I::N, R = I::R, T = I::T, G = R / C, NT = C * B;
+   static constexpr int THREADS = T;
+   static constexpr bool HAS_FILTER = MID != Mid::NONE;
+   static constexpr size_t X_BYTES = (size_t)B * sizeof(float2);
+   static constexpr size_t F_BYTES = (HAS_FILTER && FLT == Flt::SMEM) ? (size_t)B * sizeof(float2) : 0;
+   static constexpr size_t SMEM = X_BYTES + F_BYTES;
+   static_assert(C == 2 || C == 4 || C == 8 || C == 16, "outer radix");
+   static_assert(R % C == 0 && (B / C) == G * T, "each thread holds G whole columns");
+
+   template<int p>
+   __device__ __forceinline__ static void fwd_step(float2* X, float2 (&x)[R], int lane, const float2* tw)
+   {
+      sched_fence();
+      if constexpr(p > 0) {
+         xstore<I, p - 1>(X, 0, x, lane);
+         __syncthreads();
+         xload<I, p>(X, 0, x, lane);
+      }
+      butterflies<I, p, -1>(x, lane, tw);
+   }
+   template<int p>
+   __device__ __forceinline__ static void inv_step(float2* X, float2 (&x)[R], int lane, const float2* tw)
+   {
+      sched_fence();
+      if constexpr(p < I::NP - 1) {
+         xstore<I, p + 1>(X, 0, x, lane);
+         __syncthreads();
+         xload<I, p>(X, 0, x, lane);
+      }
+      butterflies<I, p, +1>(x, lane, tw);
+   }
+   template<int... ps>
+   __device__ __forceinline__ static void fwd_all(float2* X, float2 (&x)[R], int lane, const float2* tw,
+                                                  std::integer_sequence<int, ps...>)
+   {
+      (fwd_step<ps>(X, x, lane, tw), ...);
+   }
+   template<int... ps>
+   __device__ __forceinline__ static void inv_all(float2* X, float2 (&x)[R], int lane, const float2* tw,
+                                                  std::integer_sequence<int, ps...>)
+   {
+      (inv_step<I::NP - 1 - ps>(X, x, lane, tw), ...);
+   }
+
+   // the outer radix-C pass on this thread's G columns, DIF (S=-1) or DIT (S=+1)
+   template<int S>
+   __device__ __forceinline__ static void outer(float2 (&x)[R], int c, int lane, const float2* tw)
+   {
+#pragma unroll
+      for(int s = 0; s < G; ++s) {
+         float2* u = x + s * C;
+         const int col = c * (B / C) + lane + T * s;
+         const int j = col >> OUT_SHIFT;
+         float2 w[C];
+         if constexpr(OUT_L > C) twiddle_powers<C>(__ldca(tw + tw_offset(OUT_L) + (j & (OUT_L / C - 1))), w);
+         if constexpr(S > 0 && OUT_L > C) {
+#pragma unroll
+            for(int q = 1; q < C; ++q) u[q] = cmulc(u[q], w[q]);
+         }
+         dft<C, S>(u);
+         if constexpr(S < 0 && OUT_L > C) {
+#pragma unroll
+            for(int q = 1; q < C; ++q) u[q] = cmul(u[q], w[q]);
+         }
+      }
+   }
+
+   __device__ __forceinline__ static void run(const ConvArgs& args)
+   {
+      extern __shared__ __align__(1024) unsigned char smem_raw[];
+      __shared__ uint64_t fbar;
+      float2* X = reinterpret_cast<float2*>(smem_raw);
+      float2* F = reinterpret_cast<float2*>(smem_raw + X_BYTES);
+      const int lane = threadIdx.x;
+      const int c = (int)cluster_ctarank();
+      const long long tr = cluster_id_x();
+      const size_t gbase = (size_t)tr * NT;
+
+      // ---- this CTA's filter block (row c of the chain order), TMA bulk prefetch
+      if constexpr(HAS_FILTER && FLT == Flt::SMEM) {
+         if(lane == 0) {
+            mbar_init(&fbar, 1);
+            fence_mbar_init();
+         }
+         __syncthreads();
+         if(lane == 0) {
+            mbar_expect_tx(&fbar, (uint32_t)(B * 8));
+            bulk_g2s(F, static_cast<const float2*>(args.b) + (size_t)(tr * args.filter_stride) + (size_t)c * B,
+                     (uint32_t)(B * 8), &fbar);
+         }
+      }
+
+      // ---- 1. outer DIF pass on this CTA's columns, taps straight from HBM
+      float2 x[R];
+#pragma unroll
+      for(int s = 0; s < G; ++s)
+#pragma unroll
+         for(int q = 0; q < C; ++q)
+            x[s * C + q] = ld_stream(static_cast<const float2*>(args.a) + gbase + (size_t)q * B + c * (B / C) + lane +
+                                     T * s);
+      outer<-1>(x, c, lane, args.tw);
+
+      // ---- 2. push row q's values to CTA q (natural positions of the row)
+#pragma unroll
+      for(int s = 0; s < G; ++s) {
+         const uint32_t la = smem_u32(X + swz(c * (B / C) + lane + T * s));
+#pragma unroll
+         for(int q = 0; q < C; ++q) st_remote(map_remote(la, q), x[s * C + q]);
+      }
+      cluster_sync();
+
+      // ---- 3. the fused one-CTA convolution of row c
+      {
+         constexpr int r0 = I::radix(0), G0 = R / r0;
+#pragma unroll
+         for(int s = 0; s < G0; ++s)
+#pragma unroll
+            for(int k = 0; k < r0; ++k) x[s * r0 + k] = X[swz(lane + T * (s + G0 * k))];
+      }
+      fwd_all(X, x, lane, args.tw, std::make_integer_sequence<int, I::NP>{});
+      if constexpr(HAS_FILTER) {
+         float2 f[R];
+         if constexpr(FLT == Flt::SMEM) {
+            mbar_wait(&fbar, 0, args.status);
+#pragma unroll
+            for(int k = 0; k < R; ++k) f[k] = F[lane + k * T];
+         } else {
+            const float4* fp = reinterpret_cast<const float4*>(static_cast<const float2*>(args.b) +
+                                                               (size_t)(tr * args.filter_stride) + (size_t)c * B +
+                                                               (size_t)lane * R);
+#pragma unroll
+            for(int k = 0; k < R; k += 2) {
+               const float4 v = __ldg(fp + k / 2);
+               f[k] = make_float2(v.x, v.y);
+               f[k + 1] = make_float2(v.z, v.w);
+            }
+         }
+#pragma unroll
+         for(int k = 0; k < R; ++k) x[k] = (MID == Mid::MUL) ? cmul(x[k], f[k]) : cmulc(x[k], f[k]);
+      }
+      inv_all(X, x, lane, args.tw, std::make_integer_sequence<int, I::NP>{});
+      {
+         constexpr int r0 = I::radix(0), G0 = R / r0;
+#pragma unroll
+         for(int s = 0; s < G0; ++s)
+#pragma unroll
+            for(int k = 0; k < r0; ++k) X[swz(lane + T * (s + G0 * k))] = x[s * r0 + k];
+      }
+      cluster_sync();
+
+      // ---- 4. pull this CTA's columns of every row, outer DIT pass, store
+#pragma unroll
+      for(int s = 0; s < G; ++s) {
+         const uint32_t la = smem_u32(X + swz(c * (B / C) + lane + T * s));
+#pragma unroll
+         for(int q = 0; q < C; ++q) x[s * C + q] = ld_remote(map_remote(la, q));
+      }
+      cluster_sync();   // no CTA leaves while a peer may still read its buffer
+      outer<+1>(x, c, lane, args.tw);
+#pragma unroll
+      for(int s = 0; s < G; ++s)
+#pragma unroll
+         for(int q = 0; q < C; ++q)
+            st_stream(static_cast<float2*>(args.out) + gbase + (size_t)q * B + c * (B / C) + lane + T * s,
+                      x[s * C + q]);
+   }
+};
+
+template<class Inner, int C, int OUT_L, int OUT_SHIFT, Mid MID, Flt FLT>
+__global__ void __launch_bounds__(Inner::T, (Inner::T <= 256 ? 2 : 1))
+conv_cluster_kernel(const ConvArgs args)
+{
+   ClusterConv<Inner, C, OUT_L, OUT_SHIFT, MID, FLT>::run(args);
+}
+
+}  // namespace fufft

@@ -235,6 +235,14 @@ fufft_status family_mid_bfpfilter_r16(int, fufft_midop, bool, const ConvArgs&, c
 // (fp32 bits); leaves scale = max(mx, 1e-30) / 32767
 fufft_status bfp_requantize(const float2* x, float* scale, uint32_t* q, long long n, long long batch, cudaStream_t st);
 bool conv2d_supported_r16(int h, int w);
+// cluster-fused convolutions (fufft_cluster.cu); FUFFT_ERR_UNSUPPORTED when the
+// device cannot host the cluster
+fufft_status cluster_conv1d(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev);
+fufft_status cluster_large(int r_out, int mid_n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st,
+                           int dev);
+fufft_status cluster_conv2d(int h, int w, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev);
+bool cluster_conv2d_shape(int h, int w);
+constexpr int MAX_N_CLUSTER = 65536;   // radix-16 layouts, one cluster-fused kernel
 
 }  // namespace host
 }  // namespace fufft

@@ -193,6 +193,23 @@ fufft_status fufft_conv_large_f32(float* buf, const float* b, int64_t n, int64_t
    if((s = device_ctx(&c)) != FUFFT_OK) return s;
    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
    float2* x = reinterpret_cast<float2*>(buf);
+   if(lout == 1 && layout_radix(layout) == 16) {
+      // one outer level: the cluster-fused kernel does the whole four-step in
+      // one launch and 3 HBM passes (it reads every input of a transform
+      // before its first cluster barrier and writes after its last, so in
+      // place is safe); fall through to the multi-kernel form if the device
+      // cannot host the cluster
+      ConvArgs ca{};
+      ca.tw = c.tw;
+      ca.status = c.status;
+      ca.batch = batch;
+      ca.a = buf;
+      ca.out = buf;
+      ca.b = b;
+      ca.filter_stride = n;
+      s = cluster_large(r_out, mid, midop, layout_bperm(layout), ca, st, c.device);
+      if(s != FUFFT_ERR_UNSUPPORTED) return s;
+   }
    OuterArgs oa{};
    oa.dst = x;
    oa.src = x;

@@ -160,6 +160,7 @@ __host__ __device__ inline long long chain_rev_dev(long long idx, const int* w, 
 }
 
 struct PermPlan {
+   long long blk = 0;  // > 0: register-boundary order applies per block of blk points
    int w[32];          // row-dimension (W) chain: bit-group widths in pass order
    int p = 0, m = 0;
    int wh[32];         // column-dimension (H) chain; ph = 0 for 1-D
@@ -194,6 +195,14 @@ static fufft_status make_perm_plan2(int h, int wd, fufft_layout layout, PermPlan
    if(s != FUFFT_OK) return s;
    pl->v = host::layout_bperm(layout) ? R : 1;
    pl->T = h * wd / pl->v;
+   // transforms beyond one CTA run as a cluster of C CTAs, C = the first radix
+   // of the chain; each CTA's block of n/C points is its own register boundary
+   if(pl->v > 1 && (long long)h * wd > host::MAX_N_R16 && R == 16) {
+      int rad[32];
+      const int first = h > 1 ? (fufft_chain(h, R, rad), rad[0]) : (fufft_chain(wd, R, rad), rad[0]);
+      pl->blk = (long long)h * wd / first;
+      pl->T = (int)(pl->blk / pl->v);
+   }
    return FUFFT_OK;
 }
 
@@ -208,8 +217,9 @@ __host__ __device__ inline long long perm_src(long long i, const PermPlan& pl)
 {
    long long c = i;
    if(pl.v > 1) {
-      const long long L = i % pl.T, k = i / pl.T;
-      c = pl.v * L + k;
+      const long long off = pl.blk > 0 ? (i / pl.blk) * pl.blk : 0, ii = i - off;
+      const long long L = ii % pl.T, k = ii / pl.T;
+      c = off + pl.v * L + k;
    }
    const long long row = c >> pl.m, col = c & ((1LL << pl.m) - 1);
    return (chain_rev_dev(row, pl.wh, pl.ph, pl.mh) << pl.m) | chain_rev_dev(col, pl.w, pl.p, pl.m);
@@ -315,7 +325,11 @@ const char* fufft_status_string(fufft_status s)
 
 const char* fufft_last_cuda_error(void) { return host::t_last_error.c_str(); }
 
-int fufft_max_n(fufft_layout layout) { return host::max_n(host::layout_radix(layout)); }
+int fufft_max_n(fufft_layout layout)
+{
+   const int R = host::layout_radix(layout);
+   return R == 16 ? host::MAX_N_CLUSTER : host::max_n(R);
+}
 
 fufft_status fufft_init(void)
 {

@@ -85,7 +85,8 @@ typedef enum fufft_layout {
 const char* fufft_status_string(fufft_status s);
 /* text of the last CUDA error seen by this host thread ("" if none) */
 const char* fufft_last_cuda_error(void);
-/* largest one-kernel n for a layout (R8*: 4096, R16*: 8192) */
+/* largest one-kernel n for a layout (R8*: 4096; R16*: 65536, above 8192 as a
+ * thread-block cluster of n/4096 CTAs exchanging through distributed shared memory) */
 int fufft_max_n(fufft_layout layout);
 /* build the current device's twiddle tables now (otherwise done on first use) */
 fufft_status fufft_init(void);

@@ -31,7 +31,7 @@ def test_host_side_calls_without_gpu():
     from fufft_b200 import ops
     assert ops.chain(4096, 16) == [16, 16, 16]
     assert ops.chain(2048, 8) == [4, 8, 8, 8]
-    assert ops.max_n(ops.LAYOUT_R16) == 8192 and ops.max_n(ops.LAYOUT_R8) == 4096
+    assert ops.max_n(ops.LAYOUT_R16) == 65536 and ops.max_n(ops.LAYOUT_R8) == 4096
     assert ctypes.string_at(ops.lib().fufft_status_string(1)).startswith(b"invalid size")
 
 
