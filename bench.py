@@ -317,6 +317,95 @@ def run_dist(args, rank, world, dist):
             "nvlink_bytes_per_gpu": 2 * 8 * plan.n_blk * (world - 1) // world}}
 
 
+def time_flushed(torch, fn, steps, warmup, flush_bytes=512 << 20):
+    """per-step device time of fn with L2 flushed (a 512 MiB write) before every
+    step, outside the timed events; for workloads that fit in L2"""
+    junk = torch.empty(flush_bytes, dtype=torch.uint8, device="cuda")
+    for _ in range(warmup):
+        fn()
+    tot = 0.0
+    for _ in range(steps):
+        junk.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        tot += e0.elapsed_time(e1)
+    return tot / steps
+
+
+def run_sweep(args):
+    """every BASELINE.json config on one GPU, one JSON line each (device time,
+    Gpoints/s, algorithmic GB/s, fraction of the measured HBM peak)"""
+    import torch
+    from fufft_b200 import ops
+    ops.init()
+    hbm, _ = peaks()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1234)
+    steps, warm = args.steps, args.warmup
+
+    def emit(cfg, ms, pts, bytes_per_pt, extra_bytes=0, **kw):
+        gbs = (bytes_per_pt * pts + extra_bytes) / (ms * 1e-3) / 1e9
+        print(json.dumps({"config": cfg, "ms": round(ms, 4), "Gpoints_s": round(pts / (ms * 1e-3) / 1e9, 2),
+                          "GB_s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 4), "bytes_per_point": bytes_per_pt,
+                          **kw}), flush=True)
+
+    # config 1: N=1024, batch 4096 (32 MiB per array: fits L2, so L2 is flushed per step)
+    n, batch = 1024, 4096
+    a = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g)
+    b = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g) / n
+    o = torch.empty_like(a)
+    for lay, name in [(ops.LAYOUT_R16_BPERM, "R16_BPERM"), (ops.LAYOUT_R16, "R16")]:
+        ms = time_flushed(torch, lambda: ops.conv(a, b, n, lay, out=o), steps, warm)
+        emit(f"1: fp32 N={n} batch={batch} {name} (L2 flushed per step)", ms, batch * n, 24)
+    del a, b, o
+    # config 2: size sweep, 1 GiB of signal, fp32 and int16-BFP
+    for n in (512, 1024, 2048, 4096):
+        batch = POINTS // n
+        a = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g)
+        b = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g) / n
+        o = torch.empty_like(a)
+        for lay, name in [(ops.LAYOUT_R16_BPERM, "R16_BPERM"), (ops.LAYOUT_R16, "R16"), (ops.LAYOUT_R8, "R8")]:
+            if n <= ops.max_n(lay):
+                ms = time_steps(torch, lambda: ops.conv(a, b, n, lay, out=o), steps, warm, None)
+                emit(f"2: fp32 N={n} {name}", ms, batch * n, 24)
+        aq, as_ = ops.bfp_pack(a, n)
+        bq, bs = ops.bfp_pack(b, n)
+        for lay, name in [(ops.LAYOUT_R16, "R16"), (ops.LAYOUT_R16_BPERM, "R16_BPERM")]:
+            ms = time_steps(torch, lambda: ops.conv_bfp(aq, as_, bq, bs, n, lay), steps, warm, None)
+            emit(f"2: int16-BFP N={n} {name}", ms, batch * n, 12, 12 * batch)
+        del a, b, o, aq, bq
+    # config 4: 2-D 256x256 x 512 images, one shared filter
+    h = w = 256
+    batch = 512
+    a = torch.rand(batch * h * w, device="cuda", generator=g).to(torch.complex64)
+    b = torch.randn(h * w, dtype=torch.complex64, device="cuda", generator=g) / (h * w)
+    o = torch.empty_like(a)
+    for lay, name in [(ops.LAYOUT_R16, "R16"), (ops.LAYOUT_R16_BPERM, "R16_BPERM")]:
+        ms = time_steps(torch, lambda: ops.conv2d(a, b, h, w, lay, filter_stride=0, out=o), steps, warm, None)
+        emit(f"4: 2-D {h}x{w} batch={batch} shared filter {name} (cluster of 16 CTAs)", ms, batch * h * w, 16, 8 * h * w)
+    del a, b, o
+    # config 5: four-step N=32768, batch 2048, fp32 (cluster-fused) and int16-BFP (multi-kernel)
+    n, batch = 32768, 2048
+    r_out, mid = ops.large_plan(n, ops.LAYOUT_R16)
+    a = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g)
+    b = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g) / n
+    buf = a.clone()
+    ms = time_steps(torch, lambda: ops.conv_large(buf, b, n, ops.LAYOUT_R16, r_out=r_out, mid_size=mid),
+                    steps, warm, None)
+    emit(f"5: fp32 four-step N={n} batch={batch} (r_out {r_out}, mid {mid}: one cluster kernel)", ms, batch * n, 24)
+    ms = time_steps(torch, lambda: ops.conv(a, b, n, ops.LAYOUT_R16, out=buf), steps, warm, None)
+    emit(f"5: fp32 N={n} batch={batch} radix-16 chain (cluster of 8 CTAs)", ms, batch * n, 24)
+    aq, as_ = ops.bfp_pack(a, n)
+    bq, bs = ops.bfp_pack(b, n)
+    ws = torch.empty(batch * n * 8, dtype=torch.uint8, device="cuda")
+    ms = time_steps(torch, lambda: ops.conv_large_bfp(aq, as_, bq, bs, n, ops.LAYOUT_R16, workspace=ws),
+                    steps, warm, None)
+    emit(f"5: int16-BFP four-step N={n} batch={batch} (multi-kernel, fp32 workspace)", ms, batch * n, 12, 12 * batch)
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return None
@@ -351,11 +440,15 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=1.0, help="per-thread sample per reference step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-case", action="store_true", help="one launch per headline kernel, for ncu")
-    ap.add_argument("--workload", choices=["batch", "dist"], default="batch",
-                    help="dist: one 2^26-point signal over all ranks (2, 4 or 8)")
+    ap.add_argument("--workload", choices=["batch", "dist", "sweep"], default="batch",
+                    help="dist: one 2^26-point signal over all ranks (2, 4 or 8); sweep: every "
+                         "BASELINE.json config on one GPU, one JSON line each")
     args = ap.parse_args()
     if args.ncu_case:
         run_ncu_case()
+        return
+    if args.workload == "sweep":
+        run_sweep(args)
         return
     args.warmup = max(args.warmup, 3)
 

@@ -129,9 +129,8 @@ __device__ __forceinline__ void butterflies(float2 (&x)[C::R], int lane, const f
       float2* u = x + s * r;
       if constexpr(C::tw_on(p)) {
          const int j = ((lane + s * T) & (M - 1)) >> C::tw_shift(p);
-         const float2 w1 = __ldca(twt + tw_offset(C::tw_L(p)) + j);
          float2 w[r];
-         twiddle_powers<r>(w1, w);
+         twiddle_powers<r>(__ldca(twt + tw_offset(C::tw_L(p)) + j), w);
          if constexpr(S > 0) {
 #pragma unroll
             for(int k = 1; k < r; ++k) u[k] = cmulc(u[k], w[k]);
@@ -207,11 +206,20 @@ __device__ __forceinline__ float2 bfp_dequant(uint32_t w, float scale)
 {
    return make_float2((float)(short)(w & 0xffffu) * scale, (float)(short)(w >> 16) * scale);
 }
+// rint(clamp(v * inv, +-32767)) per component.  The float -> s16 conversion
+// saturates by definition, and |v * inv| <= 32767 * (1 + 2^-23) because inv
+// comes from the abs-max of the same values, so the explicit clamp of the
+// reference's C++ form (fufft.cuh:1587-1589) changes nothing reachable; the
+// reference's own PTX form (fufft.cuh:1576-1584) uses the same conversion.
 __device__ __forceinline__ uint32_t bfp_quant(float2 v, float inv)
 {
-   const int qx = __float2int_rn(fminf(fmaxf(v.x * inv, -32767.0f), 32767.0f));
-   const int qy = __float2int_rn(fminf(fmaxf(v.y * inv, -32767.0f), 32767.0f));
-   return ((uint32_t)(uint16_t)qy << 16) | (uint16_t)qx;
+   uint32_t r;
+   asm("{\n\t.reg .s16 sx, sy;\n\t.reg .f32 fx, fy;\n\t"
+       "mul.rn.f32 fx, %1, %3;\n\tmul.rn.f32 fy, %2, %3;\n\t"
+       "cvt.rni.s16.f32 sx, fx;\n\tcvt.rni.s16.f32 sy, fy;\n\t"
+       "mov.b32 %0, {sx, sy};\n\t}"
+       : "=r"(r) : "f"(v.x), "f"(v.y), "f"(inv));
+   return r;
 }
 
 template<class C_, int CPB, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>

@@ -20,8 +20,25 @@ namespace fufft {
 // ---------------------------------------------------------------------------
 // complex fp32 on float2 = (re, im)
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
-__device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+// sm_100 packed fp32 pair arithmetic: one instruction per complex add/sub
+// (per-lane IEEE add, bit-identical to the scalar form).  Measured on B200:
+// +5..10% on the fused convolution, which is issue-bound, not FMA-pipe-bound.
+__device__ __forceinline__ float2 cadd(float2 a, float2 b)
+{
+   float2 r;
+   asm("{\n\t.reg .b64 ra, rb, rr;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+       "add.rn.f32x2 rr, ra, rb;\n\tmov.b64 {%0, %1}, rr;\n\t}"
+       : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+   return r;
+}
+__device__ __forceinline__ float2 csub(float2 a, float2 b)
+{
+   float2 r;
+   asm("{\n\t.reg .b64 ra, rb, rr;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+       "sub.rn.f32x2 rr, ra, rb;\n\tmov.b64 {%0, %1}, rr;\n\t}"
+       : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+   return r;
+}
 // a * w, two fused products (same rounding shape as the reference's cmul,
 // fufft.cuh:243-261)
 __device__ __forceinline__ float2 cmul(float2 a, float2 w)
