@@ -268,13 +268,28 @@ def run_ours(args, rank, world, dist):
     return line
 
 
-def run_ncu_case():
-    """one launch of each headline kernel on a half-size batch (512 MiB signal,
-    still > L2), for ncu: fp32 (register-boundary filter), fp32 (linear chain
-    filter), int16-BFP (linear chain filter)"""
+def run_ncu_case(which: str = "headline"):
+    """one launch of each kernel of a group, on a batch of a few hundred MB
+    (> L2), for ncu.  headline: fp32 (register-boundary filter), fp32 (linear
+    chain filter), int16-BFP (linear chain filter) at N=4096; cluster: the
+    cluster-fused N=32768 (radix-16 chain and the four-step recipe) and 2-D
+    256x256"""
     import torch
     from fufft_b200 import ops
     ops.init()
+    if which == "cluster":
+        g = torch.Generator(device="cuda")
+        g.manual_seed(0)
+        n, batch = 32768, 1024
+        a = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g)
+        b = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g) / n
+        o = torch.empty_like(a)
+        ops.conv(a, b, n, ops.LAYOUT_R16_BPERM, out=o)
+        ops.conv_large(o, b, n, ops.LAYOUT_R16_BPERM, r_out=16, mid_size=2048)
+        ops.conv2d(a, b[:65536], 256, 256, ops.LAYOUT_R16_BPERM, filter_stride=0, out=o)
+        torch.cuda.synchronize()
+        assert ops.device_status() == 0
+        return
     n, batch = N, POINTS // N // 2
     g = torch.Generator(device="cuda")
     g.manual_seed(0)
@@ -439,13 +454,14 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=2.0, help="per-thread CPU baseline sample")
     ap.add_argument("--ref-seconds", type=float, default=1.0, help="per-thread sample per reference step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--ncu-case", action="store_true", help="one launch per headline kernel, for ncu")
+    ap.add_argument("--ncu-case", nargs="?", const="headline", default=None, choices=["headline", "cluster"],
+                    help="one launch per kernel of a group, for ncu")
     ap.add_argument("--workload", choices=["batch", "dist", "sweep"], default="batch",
                     help="dist: one 2^26-point signal over all ranks (2, 4 or 8); sweep: every "
                          "BASELINE.json config on one GPU, one JSON line each")
     args = ap.parse_args()
     if args.ncu_case:
-        run_ncu_case()
+        run_ncu_case(args.ncu_case)
         return
     if args.workload == "sweep":
         run_sweep(args)

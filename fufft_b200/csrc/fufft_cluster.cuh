@@ -14,8 +14,11 @@
 //      fufft_conv.cuh: DIF chain, filter block q at the register boundary,
 //      DIT chain), result back into its own buffer, cluster barrier;
 //   4. pull: CTA c reads its columns of every row from the other CTAs
-//      (ld.shared::cluster), cluster barrier (nobody exits while a peer still
-//      reads its memory), radix-C DIT pass in registers, coalesced stores.
+//      (ld.shared::cluster), radix-C DIT pass in registers, coalesced stores;
+//      a split-phase cluster barrier around the stores keeps every CTA alive
+//      until its peers have read its buffer.
+// A relaxed arrive at kernel start, waited on before the first push, makes
+// sure every CTA of the cluster runs before its shared memory is written.
 // The filter of the whole transform is in the chain order [C] ++ inner chain;
 // its block q is exactly the inner transform's own chain-ordered filter.
 // 1-D: N = 16384 (C 4), 32768 (C 8), 65536 (C 16) with B = 4096 and the
@@ -45,6 +48,15 @@ __device__ __forceinline__ uint32_t cluster_id_x()
 __device__ __forceinline__ void cluster_sync()
 {
    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// split-phase forms: arrive early, wait late, with independent work between
+__device__ __forceinline__ void cluster_arrive_relaxed()
+{
+   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait()
+{
+   asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
 }
 // shared::cta address of this CTA -> the same offset in CTA `rank` of the cluster
 __device__ __forceinline__ uint32_t map_remote(uint32_t local_addr, uint32_t rank)
@@ -147,6 +159,10 @@ struct ClusterConv {
       const long long tr = cluster_id_x();
       const size_t gbase = (size_t)tr * NT;
 
+      // every CTA of the cluster must be running before any touches a peer's
+      // shared memory: arrive now, wait just before the first push
+      cluster_arrive_relaxed();
+
       // ---- this CTA's filter block (row c of the chain order), TMA bulk prefetch
       if constexpr(HAS_FILTER && FLT == Flt::SMEM) {
          if(lane == 0) {
@@ -170,6 +186,7 @@ struct ClusterConv {
             x[s * C + q] = ld_stream(static_cast<const float2*>(args.a) + gbase + (size_t)q * B + c * (B / C) + lane +
                                      T * s);
       outer<-1>(x, c, lane, args.tw);
+      cluster_wait();
 
       // ---- 2. push row q's values to CTA q (natural positions of the row)
 #pragma unroll
@@ -226,14 +243,17 @@ struct ClusterConv {
 #pragma unroll
          for(int q = 0; q < C; ++q) x[s * C + q] = ld_remote(map_remote(la, q));
       }
-      cluster_sync();   // no CTA leaves while a peer may still read its buffer
       outer<+1>(x, c, lane, args.tw);
+      // the pulled values are consumed: announce it, store, and only then wait
+      // -- no CTA leaves while a peer may still read its buffer
+      cluster_arrive_relaxed();
 #pragma unroll
       for(int s = 0; s < G; ++s)
 #pragma unroll
          for(int q = 0; q < C; ++q)
             st_stream(static_cast<float2*>(args.out) + gbase + (size_t)q * B + c * (B / C) + lane + T * s,
                       x[s * C + q]);
+      cluster_wait();
    }
 };
 
