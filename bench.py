@@ -360,6 +360,7 @@ def run_sweep(args):
     g = torch.Generator(device="cuda")
     g.manual_seed(1234)
     steps, warm = args.steps, args.warmup
+    cfgs = {int(c) for c in args.configs.split(",")}
 
     def emit(cfg, ms, pts, bytes_per_pt, extra_bytes=0, **kw):
         gbs = (bytes_per_pt * pts + extra_bytes) / (ms * 1e-3) / 1e9
@@ -368,57 +369,85 @@ def run_sweep(args):
                           **kw}), flush=True)
 
     # config 1: N=1024, batch 4096 (32 MiB per array: fits L2, so L2 is flushed per step)
-    n, batch = 1024, 4096
-    a = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g)
-    b = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g) / n
-    o = torch.empty_like(a)
-    for lay, name in [(ops.LAYOUT_R16_BPERM, "R16_BPERM"), (ops.LAYOUT_R16, "R16")]:
-        ms = time_flushed(torch, lambda: ops.conv(a, b, n, lay, out=o), steps, warm)
-        emit(f"1: fp32 N={n} batch={batch} {name} (L2 flushed per step)", ms, batch * n, 24)
-    del a, b, o
-    # config 2: size sweep, 1 GiB of signal, fp32 and int16-BFP
-    for n in (512, 1024, 2048, 4096):
-        batch = POINTS // n
+    if 1 in cfgs:
+        n, batch = 1024, 4096
         a = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g)
         b = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g) / n
         o = torch.empty_like(a)
-        for lay, name in [(ops.LAYOUT_R16_BPERM, "R16_BPERM"), (ops.LAYOUT_R16, "R16"), (ops.LAYOUT_R8, "R8")]:
-            if n <= ops.max_n(lay):
-                ms = time_steps(torch, lambda: ops.conv(a, b, n, lay, out=o), steps, warm, None)
-                emit(f"2: fp32 N={n} {name}", ms, batch * n, 24)
+        for lay, name in [(ops.LAYOUT_R16_BPERM, "R16_BPERM"), (ops.LAYOUT_R16, "R16")]:
+            ms = time_flushed(torch, lambda: ops.conv(a, b, n, lay, out=o), steps, warm)
+            emit(f"1: fp32 N={n} batch={batch} {name} (L2 flushed per step)", ms, batch * n, 24)
+        del a, b, o
+    # config 2: size sweep, 1 GiB of signal, fp32 and int16-BFP
+    if 2 in cfgs:
+        for n in (512, 1024, 2048, 4096):
+            batch = POINTS // n
+            a = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g)
+            b = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g) / n
+            o = torch.empty_like(a)
+            for lay, name in [(ops.LAYOUT_R16_BPERM, "R16_BPERM"), (ops.LAYOUT_R16, "R16"), (ops.LAYOUT_R8, "R8")]:
+                if n <= ops.max_n(lay):
+                    ms = time_steps(torch, lambda: ops.conv(a, b, n, lay, out=o), steps, warm, None)
+                    emit(f"2: fp32 N={n} {name}", ms, batch * n, 24)
+            aq, as_ = ops.bfp_pack(a, n)
+            bq, bs = ops.bfp_pack(b, n)
+            for lay, name in [(ops.LAYOUT_R16, "R16"), (ops.LAYOUT_R16_BPERM, "R16_BPERM")]:
+                ms = time_steps(torch, lambda: ops.conv_bfp(aq, as_, bq, bs, n, lay), steps, warm, None)
+                emit(f"2: int16-BFP N={n} {name}", ms, batch * n, 12, 12 * batch)
+            del a, b, o, aq, bq
+    # config 3: 1024 real signals x 256 real filters at N=4096: packed pairs -> 512
+    # spectra (fwd once per step) -> every pair against every filter in one launch,
+    # 1024 x 256 x 4096 real outputs (4 GiB) per mid-op.  Bytes: 4 B per real output
+    # point written; spectra, filters and the signals are read once (they stay in L2)
+    if 3 in cfgs:
+        n, nsig, nfilt = 4096, 1024, 256
+        x = torch.randn(nsig * n, device="cuda", generator=g)
+        taps = torch.rand(nfilt, n, device="cuda", generator=g) * 2 - 1
+        b_nat = torch.fft.fft(taps.double(), dim=1) / n
+        bp = ops.filter_permute(b_nat.to(torch.complex64).reshape(-1), n, ops.LAYOUT_R16_BPERM)
+        xs = x.view(nsig // 2, 2, n)
+        xr, yr = xs[:, 0].contiguous().view(-1), xs[:, 1].contiguous().view(-1)
+        o = torch.empty(nsig * nfilt * n, device="cuda")
+        for mid, mname in [(ops.MID_MULTIPLY, "multiply"), (ops.MID_CONJ_MULTIPLY, "conj-multiply")]:
+            def step():
+                spec = ops.fwd_r2(xr, yr, n, ops.LAYOUT_R16_BPERM)
+                ops.apply_grid_r2(spec, bp, n, ops.LAYOUT_R16_BPERM, mid, out=o)
+            ms = time_steps(torch, step, steps, warm, None)
+            emit(f"3: real pairs N={n}: {nsig} signals x {nfilt} filters, fwd_r2 + apply_grid_r2 {mname} "
+                 f"(4 GiB out)", ms, nsig * nfilt * n, 4, 8 * n * (nsig // 2 + nfilt) + 16 * n * (nsig // 2),
+                 points="real output points")
+        del x, taps, b_nat, bp, xs, xr, yr, o
+    # config 4: 2-D 256x256 x 512 images, one shared filter
+    if 4 in cfgs:
+        h = w = 256
+        batch = 512
+        a = torch.rand(batch * h * w, device="cuda", generator=g).to(torch.complex64)
+        b = torch.randn(h * w, dtype=torch.complex64, device="cuda", generator=g) / (h * w)
+        o = torch.empty_like(a)
+        for lay, name in [(ops.LAYOUT_R16, "R16"), (ops.LAYOUT_R16_BPERM, "R16_BPERM")]:
+            ms = time_steps(torch, lambda: ops.conv2d(a, b, h, w, lay, filter_stride=0, out=o), steps, warm, None)
+            emit(f"4: 2-D {h}x{w} batch={batch} shared filter {name} (cluster of 16 CTAs)", ms, batch * h * w, 16, 8 * h * w)
+        del a, b, o
+    # config 5: four-step N=32768, batch 2048, fp32 (cluster-fused) and int16-BFP (multi-kernel)
+    if 5 in cfgs:
+        n, batch = 32768, 2048
+        r_out, mid = ops.large_plan(n, ops.LAYOUT_R16)
+        a = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g)
+        b = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g) / n
+        buf = a.clone()
+        for lay, name in [(ops.LAYOUT_R16, "R16"), (ops.LAYOUT_R16_BPERM, "R16_BPERM")]:
+            ms = time_steps(torch, lambda: ops.conv_large(buf, b, n, lay, r_out=r_out, mid_size=mid),
+                            steps, warm, None)
+            emit(f"5: fp32 four-step N={n} batch={batch} {name} (r_out {r_out}, mid {mid}: one cluster kernel)",
+                 ms, batch * n, 24)
+            ms = time_steps(torch, lambda: ops.conv(a, b, n, lay, out=buf), steps, warm, None)
+            emit(f"5: fp32 N={n} batch={batch} {name} radix-16 chain (cluster of 8 CTAs)", ms, batch * n, 24)
         aq, as_ = ops.bfp_pack(a, n)
         bq, bs = ops.bfp_pack(b, n)
-        for lay, name in [(ops.LAYOUT_R16, "R16"), (ops.LAYOUT_R16_BPERM, "R16_BPERM")]:
-            ms = time_steps(torch, lambda: ops.conv_bfp(aq, as_, bq, bs, n, lay), steps, warm, None)
-            emit(f"2: int16-BFP N={n} {name}", ms, batch * n, 12, 12 * batch)
-        del a, b, o, aq, bq
-    # config 4: 2-D 256x256 x 512 images, one shared filter
-    h = w = 256
-    batch = 512
-    a = torch.rand(batch * h * w, device="cuda", generator=g).to(torch.complex64)
-    b = torch.randn(h * w, dtype=torch.complex64, device="cuda", generator=g) / (h * w)
-    o = torch.empty_like(a)
-    for lay, name in [(ops.LAYOUT_R16, "R16"), (ops.LAYOUT_R16_BPERM, "R16_BPERM")]:
-        ms = time_steps(torch, lambda: ops.conv2d(a, b, h, w, lay, filter_stride=0, out=o), steps, warm, None)
-        emit(f"4: 2-D {h}x{w} batch={batch} shared filter {name} (cluster of 16 CTAs)", ms, batch * h * w, 16, 8 * h * w)
-    del a, b, o
-    # config 5: four-step N=32768, batch 2048, fp32 (cluster-fused) and int16-BFP (multi-kernel)
-    n, batch = 32768, 2048
-    r_out, mid = ops.large_plan(n, ops.LAYOUT_R16)
-    a = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g)
-    b = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g) / n
-    buf = a.clone()
-    ms = time_steps(torch, lambda: ops.conv_large(buf, b, n, ops.LAYOUT_R16, r_out=r_out, mid_size=mid),
-                    steps, warm, None)
-    emit(f"5: fp32 four-step N={n} batch={batch} (r_out {r_out}, mid {mid}: one cluster kernel)", ms, batch * n, 24)
-    ms = time_steps(torch, lambda: ops.conv(a, b, n, ops.LAYOUT_R16, out=buf), steps, warm, None)
-    emit(f"5: fp32 N={n} batch={batch} radix-16 chain (cluster of 8 CTAs)", ms, batch * n, 24)
-    aq, as_ = ops.bfp_pack(a, n)
-    bq, bs = ops.bfp_pack(b, n)
-    ws = torch.empty(batch * n * 8, dtype=torch.uint8, device="cuda")
-    ms = time_steps(torch, lambda: ops.conv_large_bfp(aq, as_, bq, bs, n, ops.LAYOUT_R16, workspace=ws),
-                    steps, warm, None)
-    emit(f"5: int16-BFP four-step N={n} batch={batch} (multi-kernel, fp32 workspace)", ms, batch * n, 12, 12 * batch)
+        ws = torch.empty(batch * n * 8, dtype=torch.uint8, device="cuda")
+        ms = time_steps(torch, lambda: ops.conv_large_bfp(aq, as_, bq, bs, n, ops.LAYOUT_R16, workspace=ws),
+                        steps, warm, None)
+        emit(f"5: int16-BFP four-step N={n} batch={batch} (multi-kernel, fp32 workspace)", ms, batch * n, 12, 12 * batch)
 
 
 def run_reference(args, rank, world):
@@ -456,6 +485,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-case", nargs="?", const="headline", default=None, choices=["headline", "cluster"],
                     help="one launch per kernel of a group, for ncu")
+    ap.add_argument("--configs", default="1,2,3,4,5", help="sweep: which BASELINE.json configs (1-based)")
     ap.add_argument("--workload", choices=["batch", "dist", "sweep"], default="batch",
                     help="dist: one 2^26-point signal over all ranks (2, 4 or 8); sweep: every "
                          "BASELINE.json config on one GPU, one JSON line each")

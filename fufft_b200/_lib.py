@@ -38,6 +38,9 @@ SIGNATURES = {
     "fufft_conv2d_f32": (_I, [_P, _P, _P, _I, _I, _I64, _I, _I, _I64, _P]),
     "fufft_fwd_f32": (_I, [_P, _P, _I, _I64, _I, _P]),
     "fufft_apply_f32": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I64, _I64, _P]),
+    "fufft_fwd_r2_f32": (_I, [_P, _P, _P, _I, _I64, _I, _P]),
+    "fufft_apply_grid_f32": (_I, [_P, _I64, _P, _I64, _P, _I, _I, _I, _P]),
+    "fufft_apply_grid_r2_f32": (_I, [_P, _I64, _P, _I64, _P, _I, _I, _I, _P]),
     "fufft_conv_r2_f32": (_I, [_P, _P, _P, _P, _P, _I, _I64, _I, _I, _I64, _P]),
     "fufft_bfp_pack": (_I, [_P, _P, _P, _I, _I64, _P]),
     "fufft_bfp_unpack": (_I, [_P, _P, _P, _I, _I64, _P]),

@@ -97,7 +97,7 @@ fufft_status fufft_fwd_f32(const float* a, float* spec, int n, int64_t batch, fu
    args.a = a;
    args.out = spec;
    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-   return (R == 8 ? family_fwd_r8 : family_fwd_r16)(n, FUFFT_MID_NONE, false, args, st, dev);
+   return (R == 8 ? family_fwd_r8 : family_fwd_r16)(n, FUFFT_MID_NONE, layout_bperm(layout), args, st, dev);
 }
 
 fufft_status fufft_apply_f32(const float* spec, const float* b, float* out, int n, int64_t batch,
@@ -120,6 +120,62 @@ fufft_status fufft_apply_f32(const float* spec, const float* b, float* out, int 
    args.filter_stride = filter_stride;
    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
    return (R == 8 ? family_apply_r8 : family_apply_r16)(n, mid, layout_bperm(layout), args, st, dev);
+}
+
+fufft_status fufft_fwd_r2_f32(const float* xr, const float* yr, float* spec, int n, int64_t batch,
+                              fufft_layout layout, fufft_stream_t stream)
+{
+   ConvArgs args{};
+   int R = 0, dev = 0;
+   bool skip;
+   fufft_status s = prepare(n, batch, layout, &R, &args, &dev, &skip);
+   if(s != FUFFT_OK || skip) return s;
+   if(!xr || !yr || !spec) return FUFFT_ERR_INVALID_ARG;
+   if(!aligned(xr, 4) || !aligned(yr, 4) || !aligned(spec, 16)) return FUFFT_ERR_MISALIGNED;
+   args.a = xr;
+   args.a2 = yr;
+   args.out = spec;
+   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+   return (R == 8 ? family_fwd_r2_r8 : family_fwd_r2_r16)(n, FUFFT_MID_NONE, layout_bperm(layout), args, st, dev);
+}
+
+// every spectrum x every filter in one launch: transform t = s * n_filt + f
+static fufft_status apply_grid(const float* spec, int64_t n_spec, const float* b, int64_t n_filt, float* out,
+                               int n, fufft_layout layout, fufft_midop mid, bool real_pair, fufft_stream_t stream)
+{
+   if(n_spec < 0 || n_filt < 0) return FUFFT_ERR_INVALID_BATCH;
+   if(n_filt > 0 && n_spec > ((int64_t)1 << 40) / n_filt) return FUFFT_ERR_INVALID_BATCH;
+   ConvArgs args{};
+   int R = 0, dev = 0;
+   bool skip;
+   fufft_status s = prepare(n, n_spec * n_filt, layout, &R, &args, &dev, &skip);
+   if(s != FUFFT_OK || skip) return s;
+   if(!spec || !out) return FUFFT_ERR_INVALID_ARG;
+   if(mid != FUFFT_MID_MULTIPLY && mid != FUFFT_MID_CONJ_MULTIPLY) return FUFFT_ERR_INVALID_ARG;
+   if(!aligned(spec, 16) || !aligned(out, real_pair ? 4 : 8)) return FUFFT_ERR_MISALIGNED;
+   if((s = check_filter(b, mid, n, 8)) != FUFFT_OK) return s;
+   args.a = spec;
+   args.b = b;
+   args.out = out;
+   args.filter_stride = n;
+   args.grid_filters = n_filt;
+   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+   if(!real_pair) return (R == 8 ? family_apply_r8 : family_apply_r16)(n, mid, layout_bperm(layout), args, st, dev);
+   args.out2 = out + (size_t)n_filt * n;
+   return (R == 8 ? family_apply_r2_r8 : family_apply_r2_r16)(n, mid, layout_bperm(layout), args, st, dev);
+}
+
+fufft_status fufft_apply_grid_f32(const float* spec, int64_t n_spec, const float* b, int64_t n_filt, float* out,
+                                  int n, fufft_layout layout, fufft_midop mid, fufft_stream_t stream)
+{
+   return apply_grid(spec, n_spec, b, n_filt, out, n, layout, mid, false, stream);
+}
+
+fufft_status fufft_apply_grid_r2_f32(const float* spec, int64_t n_pairs, const float* b, int64_t n_filt,
+                                     float* out, int n, fufft_layout layout, fufft_midop mid,
+                                     fufft_stream_t stream)
+{
+   return apply_grid(spec, n_pairs, b, n_filt, out, n, layout, mid, true, stream);
 }
 
 fufft_status fufft_conv_r2_f32(const float* xr, const float* yr, const float* b, float* ur, float* vr,

@@ -8,17 +8,22 @@
 // points of one column; the rest of the chain works inside rows.  So:
 //   1. CTA c loads columns c*B/C .. (c+1)*B/C - 1 of all rows straight from
 //      HBM (coalesced) and runs the radix-C DIF pass on them in registers;
-//   2. push: the value of row q goes into CTA q's shared buffer (st.shared::
-//      cluster), cluster barrier -- CTA q now holds row q;
+//   2. forward exchange: the value of row q goes to CTA q's buffer X by an
+//      asynchronous remote store (st.async) that counts its bytes on CTA q's
+//      mbarrier -- CTA q waits for its row's bytes, not for the whole cluster;
 //   3. CTA q runs the fused one-CTA convolution on its B points (the engine of
 //      fufft_conv.cuh: DIF chain, filter block q at the register boundary,
-//      DIT chain), result back into its own buffer, cluster barrier;
-//   4. pull: CTA c reads its columns of every row from the other CTAs
-//      (ld.shared::cluster), radix-C DIT pass in registers, coalesced stores;
-//      a split-phase cluster barrier around the stores keeps every CTA alive
-//      until its peers have read its buffer.
-// A relaxed arrive at kernel start, waited on before the first push, makes
-// sure every CTA of the cluster runs before its shared memory is written.
+//      DIT chain); the results stay in registers;
+//   4. return exchange: each result goes by st.async to the CTA owning its
+//      column, into that CTA's buffer Y (a third buffer, so no CTA has to wait
+//      for its peers to finish with X or with the filter), counted on a second
+//      mbarrier; radix-C DIT pass in registers, coalesced stores.
+// Each buffer is written once per kernel, so the only cluster barrier is the
+// one at start-up: a relaxed arrive after the mbarriers are initialised
+// (fence.mbarrier_init), waited on before the first remote store, which makes
+// sure every CTA of the cluster runs and can count bytes before any is sent.
+// After the return exchange no CTA touches a peer's memory, and every CTA has
+// received all bytes addressed to it before it leaves.
 // The filter of the whole transform is in the chain order [C] ++ inner chain;
 // its block q is exactly the inner transform's own chain-ordered filter.
 // 1-D: N = 16384 (C 4), 32768 (C 8), 65536 (C 16) with B = 4096 and the
@@ -27,7 +32,8 @@
 // B = 2048, chain [16, 8, 16, 16]);
 // 2-D: the first column pass is the outer pass (per-column stride H/C,
 // twiddle index = row position inside the column group).
-// Cluster barriers are reached by every thread of every CTA on every path.
+// Every bounded mbarrier wait returns (reporting a timeout in the status
+// word), so every thread of every CTA reaches the start-up barrier's wait.
 #pragma once
 #include "fufft_conv.cuh"
 
@@ -45,10 +51,6 @@ __device__ __forceinline__ uint32_t cluster_id_x()
    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
    return r;
 }
-__device__ __forceinline__ void cluster_sync()
-{
-   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
 // split-phase forms: arrive early, wait late, with independent work between
 __device__ __forceinline__ void cluster_arrive_relaxed()
 {
@@ -65,15 +67,12 @@ __device__ __forceinline__ uint32_t map_remote(uint32_t local_addr, uint32_t ran
    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
    return r;
 }
-__device__ __forceinline__ void st_remote(uint32_t addr, float2 v)
+// asynchronous remote store of 8 bytes, counted on the destination CTA's
+// mbarrier `mbar` (a shared::cluster address in that CTA)
+__device__ __forceinline__ void st_async(uint32_t addr, float2 v, uint32_t mbar)
 {
-   asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" :: "r"(addr), "f"(v.x), "f"(v.y) : "memory");
-}
-__device__ __forceinline__ float2 ld_remote(uint32_t addr)
-{
-   float2 v;
-   asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
-   return v;
+   asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];"
+                :: "r"(addr), "f"(v.x), "f"(v.y), "r"(mbar) : "memory");
 }
 
 // Inner: the one-CTA chain of a row (Chain2); C: outer radix = CTAs per
@@ -84,9 +83,13 @@ struct ClusterConv {
    static constexpr int B = I::N, R = I::R, T = I::T, G = R / C, NT = C * B;
    static constexpr int THREADS = T;
    static constexpr bool HAS_FILTER = MID != Mid::NONE;
+   static constexpr int CB = B / C;   // columns per CTA
    static constexpr size_t X_BYTES = (size_t)B * sizeof(float2);
    static constexpr size_t F_BYTES = (HAS_FILTER && FLT == Flt::SMEM) ? (size_t)B * sizeof(float2) : 0;
-   static constexpr size_t SMEM = X_BYTES + F_BYTES;
+   static constexpr size_t Y_BYTES = (size_t)B * sizeof(float2);
+   static constexpr size_t SMEM = X_BYTES + F_BYTES + Y_BYTES;
+   // bytes each exchange brings into a CTA from its C-1 peers
+   static constexpr uint32_t XCHG_BYTES = (uint32_t)((C - 1) * CB * sizeof(float2));
    static_assert(C == 2 || C == 4 || C == 8 || C == 16, "outer radix");
    static_assert(R % C == 0 && (B / C) == G * T, "each thread holds G whole columns");
 
@@ -151,25 +154,30 @@ struct ClusterConv {
    __device__ __forceinline__ static void run(const ConvArgs& args)
    {
       extern __shared__ __align__(1024) unsigned char smem_raw[];
-      __shared__ uint64_t fbar;
+      __shared__ uint64_t fbar, xbar[2];   // filter copy; forward and return exchanges
       float2* X = reinterpret_cast<float2*>(smem_raw);
       float2* F = reinterpret_cast<float2*>(smem_raw + X_BYTES);
+      float2* Y = reinterpret_cast<float2*>(smem_raw + X_BYTES + F_BYTES);
       const int lane = threadIdx.x;
       const int c = (int)cluster_ctarank();
       const long long tr = cluster_id_x();
       const size_t gbase = (size_t)tr * NT;
 
-      // every CTA of the cluster must be running before any touches a peer's
-      // shared memory: arrive now, wait just before the first push
+      // ---- mbarriers: initialised and armed (one arrival + the bytes the
+      // peers will send) before this CTA announces itself to the cluster
+      if(lane == 0) {
+         if constexpr(HAS_FILTER && FLT == Flt::SMEM) mbar_init(&fbar, 1);
+         mbar_init(&xbar[0], 1);
+         mbar_init(&xbar[1], 1);
+         fence_mbar_init();
+         mbar_expect_tx(&xbar[0], XCHG_BYTES);
+         mbar_expect_tx(&xbar[1], XCHG_BYTES);
+      }
+      __syncthreads();
       cluster_arrive_relaxed();
 
       // ---- this CTA's filter block (row c of the chain order), TMA bulk prefetch
       if constexpr(HAS_FILTER && FLT == Flt::SMEM) {
-         if(lane == 0) {
-            mbar_init(&fbar, 1);
-            fence_mbar_init();
-         }
-         __syncthreads();
          if(lane == 0) {
             mbar_expect_tx(&fbar, (uint32_t)(B * 8));
             bulk_g2s(F, static_cast<const float2*>(args.b) + (size_t)(tr * args.filter_stride) + (size_t)c * B,
@@ -183,19 +191,27 @@ struct ClusterConv {
       for(int s = 0; s < G; ++s)
 #pragma unroll
          for(int q = 0; q < C; ++q)
-            x[s * C + q] = ld_stream(static_cast<const float2*>(args.a) + gbase + (size_t)q * B + c * (B / C) + lane +
+            x[s * C + q] = ld_stream(static_cast<const float2*>(args.a) + gbase + (size_t)q * B + c * CB + lane +
                                      T * s);
       outer<-1>(x, c, lane, args.tw);
-      cluster_wait();
+      cluster_wait();   // every CTA of the cluster runs, its mbarriers armed
 
-      // ---- 2. push row q's values to CTA q (natural positions of the row)
+      // ---- 2. forward exchange: (row q, column col) -> X of CTA q at col
+      {
+         const uint32_t xb = smem_u32(X), mb = smem_u32(&xbar[0]);
 #pragma unroll
-      for(int s = 0; s < G; ++s) {
-         const uint32_t la = smem_u32(X + swz(c * (B / C) + lane + T * s));
+         for(int q = 0; q < C; ++q) {
+            const uint32_t rx = map_remote(xb, q), rm = map_remote(mb, q);
 #pragma unroll
-         for(int q = 0; q < C; ++q) st_remote(map_remote(la, q), x[s * C + q]);
+            for(int s = 0; s < G; ++s) {
+               const int col = c * CB + lane + T * s;
+               if(q == c) X[col] = x[s * C + q];
+               else st_async(rx + (uint32_t)(col * sizeof(float2)), x[s * C + q], rm);
+            }
+         }
       }
-      cluster_sync();
+      mbar_wait<true>(&xbar[0], 0, args.status);
+      __syncthreads();   // this CTA's own share, written by plain stores
 
       // ---- 3. the fused one-CTA convolution of row c
       {
@@ -203,7 +219,7 @@ struct ClusterConv {
 #pragma unroll
          for(int s = 0; s < G0; ++s)
 #pragma unroll
-            for(int k = 0; k < r0; ++k) x[s * r0 + k] = X[swz(lane + T * (s + G0 * k))];
+            for(int k = 0; k < r0; ++k) x[s * r0 + k] = X[lane + T * (s + G0 * k)];
       }
       fwd_all(X, x, lane, args.tw, std::make_integer_sequence<int, I::NP>{});
       if constexpr(HAS_FILTER) {
@@ -227,38 +243,43 @@ struct ClusterConv {
          for(int k = 0; k < R; ++k) x[k] = (MID == Mid::MUL) ? cmul(x[k], f[k]) : cmulc(x[k], f[k]);
       }
       inv_all(X, x, lane, args.tw, std::make_integer_sequence<int, I::NP>{});
+
+      // ---- 4. return exchange: row position p -> Y of its column's owner
+      // o = p / CB, at [row c][p % CB]
       {
          constexpr int r0 = I::radix(0), G0 = R / r0;
+         const uint32_t yb = smem_u32(Y), mb = smem_u32(&xbar[1]);
 #pragma unroll
          for(int s = 0; s < G0; ++s)
 #pragma unroll
-            for(int k = 0; k < r0; ++k) X[swz(lane + T * (s + G0 * k))] = x[s * r0 + k];
+            for(int k = 0; k < r0; ++k) {
+               const int p = lane + T * (s + G0 * k);
+               const int o = p / CB, idx = c * CB + (p % CB);
+               if(o == c) Y[idx] = x[s * r0 + k];
+               else st_async(map_remote(yb, o) + (uint32_t)(idx * sizeof(float2)), x[s * r0 + k],
+                             map_remote(mb, o));
+            }
       }
-      cluster_sync();
+      mbar_wait<true>(&xbar[1], 0, args.status);
+      __syncthreads();
 
-      // ---- 4. pull this CTA's columns of every row, outer DIT pass, store
+      // ---- 5. this CTA's columns of every row, outer DIT pass, store
 #pragma unroll
-      for(int s = 0; s < G; ++s) {
-         const uint32_t la = smem_u32(X + swz(c * (B / C) + lane + T * s));
+      for(int s = 0; s < G; ++s)
 #pragma unroll
-         for(int q = 0; q < C; ++q) x[s * C + q] = ld_remote(map_remote(la, q));
-      }
+         for(int q = 0; q < C; ++q) x[s * C + q] = Y[q * CB + lane + T * s];
       outer<+1>(x, c, lane, args.tw);
-      // the pulled values are consumed: announce it, store, and only then wait
-      // -- no CTA leaves while a peer may still read its buffer
-      cluster_arrive_relaxed();
 #pragma unroll
       for(int s = 0; s < G; ++s)
 #pragma unroll
          for(int q = 0; q < C; ++q)
-            st_stream(static_cast<float2*>(args.out) + gbase + (size_t)q * B + c * (B / C) + lane + T * s,
+            st_stream(static_cast<float2*>(args.out) + gbase + (size_t)q * B + c * CB + lane + T * s,
                       x[s * C + q]);
-      cluster_wait();
    }
 };
 
 template<class Inner, int C, int OUT_L, int OUT_SHIFT, Mid MID, Flt FLT>
-__global__ void __launch_bounds__(Inner::T, (Inner::T <= 256 ? 2 : 1))
+__global__ void __launch_bounds__(Inner::T, min_blocks<Inner::T>())
 conv_cluster_kernel(const ConvArgs args)
 {
    ClusterConv<Inner, C, OUT_L, OUT_SHIFT, MID, FLT>::run(args);

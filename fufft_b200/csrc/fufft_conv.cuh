@@ -30,8 +30,12 @@
 
 namespace fufft {
 
-enum class In { C32, BFP, REAL2, SPEC };   // signal form entering the kernel
-enum class Out { C32, BFP, REAL2, SPEC };  // result form leaving it
+// signal form entering / result form leaving the kernel.  SPEC: a spectrum in
+// chain order (thread `lane` owns the R consecutive positions R*lane ..);
+// SPEC_BP: the same spectrum in register-boundary order, position R*lane + k
+// stored at lane + k*T (the bperm filter map) -- coalesced for every warp access
+enum class In { C32, BFP, REAL2, SPEC, SPEC_BP };
+enum class Out { C32, BFP, REAL2, SPEC, SPEC_BP };
 enum class Mid { NONE, MUL, CONJ };        // pointwise operation between the transforms
 enum class Flt { NONE, SMEM, GLOBAL };     // filter read: TMA-staged register-boundary
                                            // layout, or chain order straight from HBM
@@ -92,6 +96,7 @@ struct ConvArgs {
    long long filter_stride;  // elements between consecutive transforms' filters; 0 = one shared filter
    long long spec_stride;    // SPEC input: elements between consecutive transforms' spectra
    long long scale_div;      // BFP filter scale of transform t: b_scale[t / scale_div] (0, 1: per transform)
+   long long grid_filters;   // SPEC input, > 0: transform t = s * grid_filters + f applies filter f to spectrum s
    long long batch;
    const float2* tw;         // the device's twiddle tables (tw_offset layout)
    unsigned int* status;     // device status word (bounded-wait reports)
@@ -228,11 +233,22 @@ struct ConvKernel {
    static constexpr int N = C::N, R = C::R;
    static constexpr int T = C::T;
    static constexpr int THREADS = CPB * T;
-   static constexpr bool HAS_FILTER = (MID != Mid::NONE) && (OUT != Out::SPEC);
+   static constexpr bool SPEC_IN = IN == In::SPEC || IN == In::SPEC_BP;
+   static constexpr bool SPEC_OUT = OUT == Out::SPEC || OUT == Out::SPEC_BP;
+   static constexpr bool HAS_FILTER = (MID != Mid::NONE) && !SPEC_OUT;
    static constexpr int FELEM = FBFP ? 4 : 8;
    static constexpr size_t X_BYTES = (size_t)CPB * N * sizeof(float2);
    static constexpr size_t F_BYTES = (HAS_FILTER && FLT == Flt::SMEM) ? (size_t)CPB * N * FELEM : 0;
    static constexpr size_t SMEM = X_BYTES + F_BYTES;
+
+   // element offset of transform t's filter.  Grid apply (one launch over every
+   // spectrum x every filter): filter t % F; otherwise t * filter_stride.
+   __device__ __forceinline__ static long long filter_off(const ConvArgs& args, long long t)
+   {
+      if constexpr(SPEC_IN)
+         if(args.grid_filters > 0) return (t % args.grid_filters) * N;
+      return t * args.filter_stride;
+   }
 
    template<int p>
    __device__ __forceinline__ static void fwd_step(float2* X, int off, float2 (&x)[R], int lane, int slot,
@@ -286,6 +302,17 @@ struct ConvKernel {
       const bool active = tr < args.batch;
       const int off = slot * N;
       const size_t gbase = (size_t)tr * N;
+      // grid apply: spectrum s = t / F.  Real-pair output rows: ur of pair s
+      // and filter f at row 2*s*F + f = t + s*F, vr one block of F rows later
+      long long spec_row = tr * args.spec_stride;
+      size_t obase = gbase;
+      if constexpr(SPEC_IN) {
+         if(args.grid_filters > 0) {
+            const long long sidx = tr / args.grid_filters;
+            spec_row = sidx * N;
+            if constexpr(OUT == Out::REAL2) obase = (size_t)(tr + sidx * args.grid_filters) * N;
+         }
+      }
 
       // ---- filter prefetch: one bulk copy per transform, completes on fbar
       if constexpr(HAS_FILTER && FLT == Flt::SMEM) {
@@ -300,14 +327,14 @@ struct ConvKernel {
             mbar_expect_tx(&fbar, (uint32_t)(nact * N * FELEM));
             const unsigned char* fb = static_cast<const unsigned char*>(args.b);
             for(int s = 0; s < nact; ++s)
-               bulk_g2s(F + (size_t)s * N * FELEM, fb + (size_t)((tr0 + s) * args.filter_stride) * FELEM,
+               bulk_g2s(F + (size_t)s * N * FELEM, fb + (size_t)filter_off(args, tr0 + s) * FELEM,
                         (uint32_t)(N * FELEM), &fbar);
          }
       }
 
       float2 x[R];
 
-      if constexpr(IN != In::SPEC) {
+      if constexpr(!SPEC_IN) {
          // ---- first DIF pass straight from HBM: x[s*r + k] = a[lane + T*(s + G*k)]
          constexpr int r0 = C::radix(0), G0 = R / r0;
          float sa = 1.0f;
@@ -329,24 +356,38 @@ struct ConvKernel {
             }
          fwd_all(X, off, x, lane, slot, args.tw, std::make_integer_sequence<int, C::NP>{});
       } else {
-         // ---- split apply: the chain-order spectrum enters at the boundary
-         const float4* sp = reinterpret_cast<const float4*>(static_cast<const float2*>(args.a) +
-                                                            (size_t)(tr * args.spec_stride) + (size_t)lane * R);
+         // ---- split apply: the spectrum enters at the boundary.  Default
+         // cache policy: a spectrum is usually reused (one spectrum, many
+         // filters), and an evict-first load would push it out of L2
+         const float2* sp = static_cast<const float2*>(args.a) + (size_t)spec_row;
+         if constexpr(IN == In::SPEC_BP) {
 #pragma unroll
-         for(int k = 0; k < R; k += 2) {
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if(active) v = ld_stream4(sp + k / 2);
-            x[k] = make_float2(v.x, v.y);
-            x[k + 1] = make_float2(v.z, v.w);
+            for(int k = 0; k < R; ++k) x[k] = active ? __ldg(sp + lane + k * T) : make_float2(0.f, 0.f);
+         } else {
+            const float4* sp4 = reinterpret_cast<const float4*>(sp + (size_t)lane * R);
+#pragma unroll
+            for(int k = 0; k < R; k += 2) {
+               float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+               if(active) v = __ldg(sp4 + k / 2);
+               x[k] = make_float2(v.x, v.y);
+               x[k + 1] = make_float2(v.z, v.w);
+            }
          }
       }
 
       // ---- register boundary: x[k] is the spectrum at chain position R*lane + k
-      if constexpr(OUT == Out::SPEC) {
+      if constexpr(SPEC_OUT) {
          if(active) {
-            float4* sp = reinterpret_cast<float4*>(static_cast<float2*>(args.out) + gbase + (size_t)lane * R);
+            if constexpr(OUT == Out::SPEC_BP) {
+               float2* sp = static_cast<float2*>(args.out) + gbase;
 #pragma unroll
-            for(int k = 0; k < R; k += 2) st_stream(sp + k / 2, make_float4(x[k].x, x[k].y, x[k + 1].x, x[k + 1].y));
+               for(int k = 0; k < R; ++k) st_stream(sp + lane + k * T, x[k]);
+            } else {
+               float4* sp = reinterpret_cast<float4*>(static_cast<float2*>(args.out) + gbase + (size_t)lane * R);
+#pragma unroll
+               for(int k = 0; k < R; k += 2)
+                  st_stream(sp + k / 2, make_float4(x[k].x, x[k].y, x[k + 1].x, x[k + 1].y));
+            }
          }
          return;
       } else {
@@ -365,7 +406,7 @@ struct ConvKernel {
                   for(int k = 0; k < R; ++k) f[k] = Fs[lane + k * T];
                }
             } else {
-               const size_t fbase = (size_t)(tr * args.filter_stride) + (size_t)lane * R;
+               const size_t fbase = (size_t)filter_off(args, tr) + (size_t)lane * R;
                if constexpr(FBFP) {
                   const float sb = active ? __ldg(args.b_scale + (args.filter_stride ? (args.scale_div > 1 ? tr / args.scale_div : tr) : 0)) : 0.0f;
                   const uint4* fp = reinterpret_cast<const uint4*>(static_cast<const uint32_t*>(args.b) + fbase);
@@ -427,7 +468,7 @@ struct ConvKernel {
             for(int s = 0; s < G0; ++s)
 #pragma unroll
                for(int k = 0; k < r0; ++k) {
-                  const size_t gi = gbase + lane + (size_t)T * (s + G0 * k);
+                  const size_t gi = obase + lane + (size_t)T * (s + G0 * k);
                   const float2 v = x[s * r0 + k];
                   if constexpr(OUT == Out::C32) st_stream(static_cast<float2*>(args.out) + gi, v);
                   else {

@@ -236,13 +236,22 @@ __device__ __forceinline__ void fence_proxy_async_smem()
    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// CLUSTER = true: acquire at cluster scope, for phases completed by other
+// CTAs' st.async stores (their complete_tx releases at cluster scope)
+template<bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
 {
    uint32_t ok;
-   asm volatile("{\n\t.reg .pred p;\n\t"
-                "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-                "selp.u32 %0, 1, 0, p;\n\t}"
-                : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+   if constexpr(CLUSTER)
+      asm volatile("{\n\t.reg .pred p;\n\t"
+                   "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+                   "selp.u32 %0, 1, 0, p;\n\t}"
+                   : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+   else
+      asm volatile("{\n\t.reg .pred p;\n\t"
+                   "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                   "selp.u32 %0, 1, 0, p;\n\t}"
+                   : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
    return ok != 0;
 }
 __device__ __forceinline__ uint64_t globaltimer_ns()
@@ -257,12 +266,13 @@ constexpr unsigned STATUS_TMA_TIMEOUT = 1u;   // a bounded mbarrier wait gave up
 
 // Bounded wait: gives up after `limit_ns` (2 s by default) and records it in
 // the status word instead of spinning forever.
+template<bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* status,
                                           uint64_t limit_ns = 2000000000ull)
 {
-   if(mbar_try_wait(bar, parity)) return true;
+   if(mbar_try_wait<CLUSTER>(bar, parity)) return true;
    const uint64_t t0 = globaltimer_ns();
-   while(!mbar_try_wait(bar, parity)) {
+   while(!mbar_try_wait<CLUSTER>(bar, parity)) {
       if(globaltimer_ns() - t0 > limit_ns) {
          atomicOr(status, STATUS_TMA_TIMEOUT);
          return false;
@@ -274,7 +284,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
 // streaming global loads/stores: data read or written once, kept out of L1 so
 // the twiddle tables stay resident
 __device__ __forceinline__ float2 ld_stream(const float2* p) { return __ldcs(p); }
-__device__ __forceinline__ float4 ld_stream4(const float4* p) { return __ldcs(p); }
 __device__ __forceinline__ uint32_t ld_stream(const uint32_t* p) { return __ldcs(reinterpret_cast<const unsigned int*>(p)); }
 __device__ __forceinline__ float ld_stream(const float* p) { return __ldcs(p); }
 __device__ __forceinline__ void st_stream(float2* p, float2 v) { __stcs(p, v); }

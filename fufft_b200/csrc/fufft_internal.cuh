@@ -176,6 +176,26 @@ fufft_status dispatch_mid(int n, fufft_midop mid, bool bperm, const ConvArgs& a,
    return FUFFT_ERR_INVALID_ARG;
 }
 
+// split apply: the spectrum comes in the layout family of the filter --
+// register-boundary order with the TMA-staged bperm filter, chain order with
+// the chain-order filter
+template<int R, Out OUT>
+fufft_status dispatch_apply(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
+{
+   switch(mid) {
+   case FUFFT_MID_NONE:
+      return bperm ? launch_n<R, In::SPEC_BP, OUT, Mid::NONE, Flt::NONE, false>(n, a, st, dev)
+                   : launch_n<R, In::SPEC, OUT, Mid::NONE, Flt::NONE, false>(n, a, st, dev);
+   case FUFFT_MID_MULTIPLY:
+      return bperm ? launch_n<R, In::SPEC_BP, OUT, Mid::MUL, Flt::SMEM, false>(n, a, st, dev)
+                   : launch_n<R, In::SPEC, OUT, Mid::MUL, Flt::GLOBAL, false>(n, a, st, dev);
+   case FUFFT_MID_CONJ_MULTIPLY:
+      return bperm ? launch_n<R, In::SPEC_BP, OUT, Mid::CONJ, Flt::SMEM, false>(n, a, st, dev)
+                   : launch_n<R, In::SPEC, OUT, Mid::CONJ, Flt::GLOBAL, false>(n, a, st, dev);
+   }
+   return FUFFT_ERR_INVALID_ARG;
+}
+
 // fp32 / BFP convolution.  Measured on B200 (N = 512..8192, 1 GiB signal):
 // the direct kernel (fufft_conv.cuh) is fastest whenever the filter arrives in
 // the register-boundary layout (TMA bulk prefetch) and for BFP; the
@@ -224,6 +244,10 @@ fufft_status family_fwd_r8(int, fufft_midop, bool, const ConvArgs&, cudaStream_t
 fufft_status family_fwd_r16(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
 fufft_status family_apply_r8(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
 fufft_status family_apply_r16(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
+fufft_status family_apply_r2_r8(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
+fufft_status family_apply_r2_r16(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
+fufft_status family_fwd_r2_r8(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
+fufft_status family_fwd_r2_r16(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
 fufft_status family_r2_r8(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
 fufft_status family_r2_r16(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
 fufft_status family_conv2d_r8(int h, int w, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);

@@ -4,7 +4,7 @@ namespace fufft {
 namespace host {
 fufft_status family_apply_r16(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
 {
-   return dispatch_mid<16, In::SPEC, Out::C32, false>(n, mid, bperm, a, st, dev);
+   return dispatch_apply<16, Out::C32>(n, mid, bperm, a, st, dev);
 }
 }  // namespace host
 }  // namespace fufft

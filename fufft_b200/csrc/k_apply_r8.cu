@@ -4,7 +4,7 @@ namespace fufft {
 namespace host {
 fufft_status family_apply_r8(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
 {
-   return dispatch_mid<8, In::SPEC, Out::C32, false>(n, mid, bperm, a, st, dev);
+   return dispatch_apply<8, Out::C32>(n, mid, bperm, a, st, dev);
 }
 }  // namespace host
 }  // namespace fufft

@@ -175,6 +175,46 @@ def apply(spec: torch.Tensor, b: torch.Tensor | None, n: int, layout: int = LAYO
     return out
 
 
+def fwd_r2(xr: torch.Tensor, yr: torch.Tensor, n: int, layout: int = LAYOUT_R16) -> torch.Tensor:
+    """chain-order spectra of the packed pairs xr + i*yr (two real signals per transform)"""
+    if xr.shape != yr.shape:
+        raise ValueError("xr and yr must have the same shape")
+    spec = torch.empty(xr.numel(), dtype=torch.complex64, device=xr.device)
+    check(lib().fufft_fwd_r2_f32(_ptr(xr), _ptr(yr), _ptr(spec), n, _batch(xr, n), layout, _stream()),
+          "fufft_fwd_r2_f32")
+    return spec
+
+
+def apply_grid(spec: torch.Tensor, b: torch.Tensor, n: int, layout: int = LAYOUT_R16, mid: int = MID_MULTIPLY,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """every spectrum against every filter in one launch: out[s][f] = IDFT(spec_s (x) b_f), complex"""
+    spec, bt = _complex(spec), _complex(b)
+    ns, nf = _batch(spec, n), _batch(bt, n)
+    if out is None:
+        out = torch.empty(ns * nf * n, dtype=torch.complex64, device=spec.device)
+    else:
+        out = _complex(out)
+        if out.numel() < ns * nf * n:
+            raise ValueError("out must hold n_spec * n_filt * n complex points")
+    check(lib().fufft_apply_grid_f32(_ptr(spec), ns, _ptr(bt), nf, _ptr(out), n, layout, mid, _stream()),
+          "fufft_apply_grid_f32")
+    return out
+
+
+def apply_grid_r2(spec: torch.Tensor, b: torch.Tensor, n: int, layout: int = LAYOUT_R16, mid: int = MID_MULTIPLY,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """packed real pairs x real filters: out[2s + j][f][0..n) real (j = 0: xr of pair s, 1: yr)"""
+    spec, bt = _complex(spec), _complex(b)
+    ns, nf = _batch(spec, n), _batch(bt, n)
+    if out is None:
+        out = torch.empty(2 * ns * nf * n, dtype=torch.float32, device=spec.device)
+    elif out.dtype != torch.float32 or out.numel() < 2 * ns * nf * n:
+        raise ValueError("out must be float32 with 2 * n_pairs * n_filt * n elements")
+    check(lib().fufft_apply_grid_r2_f32(_ptr(spec), ns, _ptr(bt), nf, _ptr(out), n, layout, mid, _stream()),
+          "fufft_apply_grid_r2_f32")
+    return out
+
+
 def conv_r2(xr: torch.Tensor, yr: torch.Tensor, b: torch.Tensor, n: int, layout: int = LAYOUT_R8,
             mid: int = MID_MULTIPLY, filter_stride: int | None = None):
     bt = _complex(b)

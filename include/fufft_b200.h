@@ -146,17 +146,44 @@ fufft_status fufft_conv2d_f32(const float* a, const float* b, float* out, int h,
                               fufft_stream_t stream);
 
 /* ---- split forward / apply (one signal, many filters) -------------------
- * fwd: natural-order signal -> chain-order spectrum (layout R8 or R16 picks
- * the chain).  Replaces fufft_pipeline_fwd (fufft.cuh:1343-1373).
- * apply: chain-order spectrum (x) filter -> inverse -> natural order.
- * Replaces fufft_pipeline_apply (fufft.cuh:1375-1407, multiply only there);
- * spec_stride is the element distance between consecutive transforms'
- * spectra (n, or 0 to apply many filters to one spectrum). */
+ * fwd: natural-order signal -> spectrum.  Replaces fufft_pipeline_fwd
+ * (fufft.cuh:1343-1373).  The spectrum's order follows the layout, like a
+ * filter's: R8 / R16 give the chain (digit-reversed) order of the reference;
+ * R8_BPERM / R16_BPERM the register-boundary order of the same values
+ * (spec[L + k*T] = chain[V*L + k], T = n/V), whose loads and stores are
+ * coalesced -- the faster pair.
+ * apply: spectrum (x) filter -> inverse -> natural order, both operands in
+ * the order of `layout`.  Replaces fufft_pipeline_apply (fufft.cuh:1375-1407,
+ * multiply only there); spec_stride is the element distance between
+ * consecutive transforms' spectra (n, or 0 to apply many filters to one
+ * spectrum). */
 fufft_status fufft_fwd_f32(const float* a, float* spec, int n, int64_t batch, fufft_layout layout,
                            fufft_stream_t stream);
 fufft_status fufft_apply_f32(const float* spec, const float* b, float* out, int n, int64_t batch,
                              fufft_layout layout, fufft_midop mid, int64_t spec_stride,
                              int64_t filter_stride, fufft_stream_t stream);
+
+/* ---- the one-signal-many-filters shape at scale (no reference counterpart:
+ * the reference's apply pairs spectrum i with filter i, fufft.cuh:1393-1395)
+ * fwd_r2: two real signals as one complex transform, xr + i*yr -> spectrum
+ *   in the order of `layout`, as fufft_fwd_f32 (the two-for-one packing of
+ *   fufft_conv_r2, fufft.cuh:1283-1290, stopped at the register boundary).
+ * apply_grid: every spectrum s < n_spec against every filter f < n_filt in one
+ *   launch; out[s][f][0..n) = IDFT(spec_s (x) b_f), complex.  Spectra and
+ *   filters are n apart, both in the order of `layout`.  mid is MULTIPLY or
+ *   CONJ_MULTIPLY.
+ * apply_grid_r2: the same for packed real pairs and REAL filters: pair s holds
+ *   real signals 2s and 2s+1, and out is real, out[2s + j][f][0..n) for
+ *   j = 0 (xr) and 1 (yr): signal i's filtered copies are rows i*n_filt ..
+ *   (i+1)*n_filt-1 of an [2*n_pairs*n_filt][n] real array.  CONJ_MULTIPLY
+ *   gives the cyclic cross-correlation with the filter. */
+fufft_status fufft_fwd_r2_f32(const float* xr, const float* yr, float* spec, int n, int64_t batch,
+                              fufft_layout layout, fufft_stream_t stream);
+fufft_status fufft_apply_grid_f32(const float* spec, int64_t n_spec, const float* b, int64_t n_filt, float* out,
+                                  int n, fufft_layout layout, fufft_midop mid, fufft_stream_t stream);
+fufft_status fufft_apply_grid_r2_f32(const float* spec, int64_t n_pairs, const float* b, int64_t n_filt,
+                                     float* out, int n, fufft_layout layout, fufft_midop mid,
+                                     fufft_stream_t stream);
 
 /* ---- two-for-one real convolution ---------------------------------------
  * Two real signals ride one complex transform (xr + i*yr); the filter must be

@@ -142,6 +142,22 @@ class Oracle:
         assert self.L.orc_apply(n, radix, mid, _ptr(spec), _ptr(b_dr), _ptr(out), spec.size // n, fs) == 0
         return out
 
+    def apply_grid(self, spec, b_dr, n: int, radix: int = 8, mid: int = MID_MULTIPLY) -> np.ndarray:
+        """every spectrum against every filter: out[s][f] = apply(spec_s, b_f), each
+        cell the reference's split apply (kernel_pipeline_apply,
+        verify_kernel.cpp:815-836) of one spectrum with one filter"""
+        spec, b_dr = _c64(spec), _c64(b_dr)
+        ns, nf = spec.size // n, b_dr.size // n
+        rows = [self.apply(np.tile(spec[s * n:(s + 1) * n], nf), b_dr, n, radix, mid) for s in range(ns)]
+        return np.concatenate(rows) if rows else np.empty(0, np.complex64)
+
+    def apply_grid_r2(self, spec, b_dr, n: int, radix: int = 8, mid: int = MID_MULTIPLY) -> np.ndarray:
+        """packed real pairs: real rows [2s + j][f] = re (j = 0) / im (j = 1) of apply_grid's [s][f]"""
+        g = self.apply_grid(spec, b_dr, n, radix, mid)
+        ns, nf = spec.size // n, b_dr.size // n
+        g = g.reshape(ns, nf, n)
+        return np.stack([g.real, g.imag], axis=1).astype(np.float32).reshape(-1)
+
     def conv_r2(self, xr, yr, b_dr, n: int, radix: int = 8, filter_stride: int | None = None):
         xr, yr, b_dr = _f32(xr), _f32(yr), _c64(b_dr)
         ur, vr = np.empty_like(xr), np.empty_like(yr)

@@ -126,8 +126,11 @@ def test_split_fwd_apply(ops, oracle, n):
             want = oracle.apply(want_spec, bdr, n, radix, mid)
             got = _host(ops.apply(spec, _dev(bdr), n, layout, mid))
             assert rel_l2(got, want) <= F32_TOL
+            # register-boundary layouts: spectrum and filter both in bperm order
+            spec_b = ops.fwd(_dev(a), n, lay_b)
+            assert rel_l2(_host(spec_b), oracle.bperm(want_spec, n, radix)) <= F32_TOL
             bp = _dev(oracle.bperm(bdr, n, radix))
-            got = _host(ops.apply(spec, bp, n, lay_b, mid))
+            got = _host(ops.apply(spec_b, bp, n, lay_b, mid))
             assert rel_l2(got, want) <= F32_TOL
         # one spectrum, many filters (spec_stride = 0)
         want = oracle.apply(np.tile(want_spec[:n], batch), bdr, n, radix)

@@ -122,3 +122,25 @@ def test_small_case_arrays_match_digests():
     for k in g.files:
         case, name = k.rsplit("/", 1)
         assert _d(g[k]) == DIG[case][name], k
+
+
+@pytest.mark.parametrize("radix", [8, 16])
+@pytest.mark.parametrize("mid", [1, 2])
+def test_oracle_apply_grid_r2_is_real_conv(oracle, radix, mid):
+    """the grid checker for packed real pairs: fwd of xr + i*yr, then apply
+    against each real filter, gives each real signal's cyclic convolution
+    (mid 1) or correlation (mid 2) with each filter (float64 numpy)"""
+    n, npair, nf = 512, 2, 3
+    rng = np.random.default_rng(91 + radix + mid)
+    x = rng.standard_normal((2 * npair, n)).astype(np.float32)
+    taps = rng.uniform(-1.0, 1.0, (nf, n))
+    b_nat = (np.fft.fft(taps, axis=1) / n).astype(np.complex64)
+    spec = oracle.fwd((x[0::2] + 1j * x[1::2]).astype(np.complex64).reshape(-1), n, radix)
+    b_dr = np.concatenate([oracle.permute_dr(b_nat[f], n, radix) for f in range(nf)])
+    got = oracle.apply_grid_r2(spec, b_dr, n, radix, mid).reshape(2 * npair, nf, n)
+    X = np.fft.fft(x.astype(np.float64), axis=1)
+    for i in range(2 * npair):
+        for f in range(nf):
+            H = np.fft.fft(taps[f])
+            ref = np.fft.ifft(X[i] * (np.conj(H) if mid == 2 else H)).real
+            assert np.linalg.norm(got[i, f] - ref) / np.linalg.norm(ref) <= 2e-5
