@@ -445,9 +445,11 @@ def run_sweep(args):
         aq, as_ = ops.bfp_pack(a, n)
         bq, bs = ops.bfp_pack(b, n)
         ws = torch.empty(batch * n * 8, dtype=torch.uint8, device="cuda")
-        ms = time_steps(torch, lambda: ops.conv_large_bfp(aq, as_, bq, bs, n, ops.LAYOUT_R16, workspace=ws),
-                        steps, warm, None)
-        emit(f"5: int16-BFP four-step N={n} batch={batch} (multi-kernel, fp32 workspace)", ms, batch * n, 12, 12 * batch)
+        for lay, name in [(ops.LAYOUT_R16, "R16"), (ops.LAYOUT_R16_BPERM, "R16_BPERM")]:
+            ms = time_steps(torch, lambda: ops.conv_large_bfp(aq, as_, bq, bs, n, lay, workspace=ws),
+                            steps, warm, None)
+            emit(f"5: int16-BFP four-step N={n} batch={batch} {name} (r_out {r_out}, mid {mid}: one cluster kernel)",
+                 ms, batch * n, 12, 12 * batch)
 
 
 def run_reference(args, rank, world):

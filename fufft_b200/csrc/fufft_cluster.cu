@@ -8,11 +8,11 @@
 namespace fufft {
 namespace host {
 
-template<class Inner, int C, int OUT_L, int OUT_SHIFT, Mid MID, Flt FLT>
+template<class Inner, int C, int OUT_L, int OUT_SHIFT, Mid MID, Flt FLT, bool BFP = false>
 static fufft_status launch_cluster(const ConvArgs& args, cudaStream_t st, int device)
 {
-   using K = ClusterConv<Inner, C, OUT_L, OUT_SHIFT, MID, FLT>;
-   auto kern = conv_cluster_kernel<Inner, C, OUT_L, OUT_SHIFT, MID, FLT>;
+   using K = ClusterConv<Inner, C, OUT_L, OUT_SHIFT, MID, FLT, BFP>;
+   auto kern = conv_cluster_kernel<Inner, C, OUT_L, OUT_SHIFT, MID, FLT, BFP>;
    static std::atomic<uint64_t> configured{0}, usable{0};
    const uint64_t bit = 1ull << (device & 63);
    cudaLaunchConfig_t cfg = {};
@@ -49,17 +49,17 @@ static fufft_status launch_cluster(const ConvArgs& args, cudaStream_t st, int de
    return s;
 }
 
-template<class Inner, int C, int OUT_L, int OUT_SHIFT>
+template<class Inner, int C, int OUT_L, int OUT_SHIFT, bool BFP = false>
 static fufft_status cluster_mid(fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
 {
    switch(mid) {
-   case FUFFT_MID_NONE: return launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::NONE, Flt::NONE>(a, st, dev);
+   case FUFFT_MID_NONE: return launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::NONE, Flt::NONE, BFP>(a, st, dev);
    case FUFFT_MID_MULTIPLY:
-      return bperm ? launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::MUL, Flt::SMEM>(a, st, dev)
-                   : launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::MUL, Flt::GLOBAL>(a, st, dev);
+      return bperm ? launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::MUL, Flt::SMEM, BFP>(a, st, dev)
+                   : launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::MUL, Flt::GLOBAL, BFP>(a, st, dev);
    case FUFFT_MID_CONJ_MULTIPLY:
-      return bperm ? launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::CONJ, Flt::SMEM>(a, st, dev)
-                   : launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::CONJ, Flt::GLOBAL>(a, st, dev);
+      return bperm ? launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::CONJ, Flt::SMEM, BFP>(a, st, dev)
+                   : launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::CONJ, Flt::GLOBAL, BFP>(a, st, dev);
    }
    return FUFFT_ERR_INVALID_ARG;
 }
@@ -83,6 +83,17 @@ fufft_status cluster_large(int r_out, int mid_n, fufft_midop mid, bool bperm, co
    if(r_out == 8 && mid_n == 2048) return cluster_mid<Chain<2048, 16>, 8, 16384, 0>(mid, bperm, a, st, dev);
    if(r_out == 16 && mid_n == 4096) return cluster_mid<Chain<4096, 16>, 16, 65536, 0>(mid, bperm, a, st, dev);
    if(r_out == 8 && mid_n == 4096) return cluster_mid<Chain<4096, 16>, 8, 32768, 0>(mid, bperm, a, st, dev);
+   return FUFFT_ERR_UNSUPPORTED;
+}
+
+// the same four-step shapes with int16-BFP signal, filter and result
+fufft_status cluster_large_bfp(int r_out, int mid_n, fufft_midop mid, bool bperm, const ConvArgs& a,
+                               cudaStream_t st, int dev)
+{
+   if(r_out == 16 && mid_n == 2048) return cluster_mid<Chain<2048, 16>, 16, 32768, 0, true>(mid, bperm, a, st, dev);
+   if(r_out == 8 && mid_n == 2048) return cluster_mid<Chain<2048, 16>, 8, 16384, 0, true>(mid, bperm, a, st, dev);
+   if(r_out == 16 && mid_n == 4096) return cluster_mid<Chain<4096, 16>, 16, 65536, 0, true>(mid, bperm, a, st, dev);
+   if(r_out == 8 && mid_n == 4096) return cluster_mid<Chain<4096, 16>, 8, 32768, 0, true>(mid, bperm, a, st, dev);
    return FUFFT_ERR_UNSUPPORTED;
 }
 

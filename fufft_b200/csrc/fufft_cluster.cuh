@@ -32,6 +32,11 @@
 // B = 2048, chain [16, 8, 16, 16]);
 // 2-D: the first column pass is the outer pass (per-column stride H/C,
 // twiddle index = row position inside the column group).
+// int16-BFP storage (BFP = true, the four-step N = r_out * mid of
+// fufft_conv_large_bfp): taps, filter block and result are packed int16 pairs
+// with one fp32 scale per transform; the output scale needs the abs-max of the
+// whole transform, so each CTA sends its own maximum to every peer (a third
+// st.async exchange of 4 bytes per peer) before quantising.
 // Every bounded mbarrier wait returns (reporting a timeout in the status
 // word), so every thread of every CTA reaches the start-up barrier's wait.
 #pragma once
@@ -74,18 +79,25 @@ __device__ __forceinline__ void st_async(uint32_t addr, float2 v, uint32_t mbar)
    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];"
                 :: "r"(addr), "f"(v.x), "f"(v.y), "r"(mbar) : "memory");
 }
+// the same for 4 bytes
+__device__ __forceinline__ void st_async(uint32_t addr, float v, uint32_t mbar)
+{
+   asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];"
+                :: "r"(addr), "r"(__float_as_uint(v)), "r"(mbar) : "memory");
+}
 
 // Inner: the one-CTA chain of a row (Chain2); C: outer radix = CTAs per
 // cluster; OUT_L / OUT_SHIFT: the outer pass's twiddle W_{OUT_L}^{(col >> OUT_SHIFT) q}
-template<class Inner, int C, int OUT_L, int OUT_SHIFT, Mid MID, Flt FLT>
+template<class Inner, int C, int OUT_L, int OUT_SHIFT, Mid MID, Flt FLT, bool BFP = false>
 struct ClusterConv {
    using I = Inner;
    static constexpr int B = I::N, R = I::R, T = I::T, G = R / C, NT = C * B;
    static constexpr int THREADS = T;
    static constexpr bool HAS_FILTER = MID != Mid::NONE;
    static constexpr int CB = B / C;   // columns per CTA
+   static constexpr int FELEM = BFP ? 4 : 8;   // filter bytes per point
    static constexpr size_t X_BYTES = (size_t)B * sizeof(float2);
-   static constexpr size_t F_BYTES = (HAS_FILTER && FLT == Flt::SMEM) ? (size_t)B * sizeof(float2) : 0;
+   static constexpr size_t F_BYTES = (HAS_FILTER && FLT == Flt::SMEM) ? (size_t)B * FELEM : 0;
    static constexpr size_t Y_BYTES = (size_t)B * sizeof(float2);
    static constexpr size_t SMEM = X_BYTES + F_BYTES + Y_BYTES;
    // bytes each exchange brings into a CTA from its C-1 peers
@@ -154,9 +166,11 @@ struct ClusterConv {
    __device__ __forceinline__ static void run(const ConvArgs& args)
    {
       extern __shared__ __align__(1024) unsigned char smem_raw[];
-      __shared__ uint64_t fbar, xbar[2];   // filter copy; forward and return exchanges
+      // filter copy; forward, return and (BFP) abs-max exchanges
+      __shared__ uint64_t fbar, xbar[3];
+      __shared__ float cmax[C], wmax[T / 32];
       float2* X = reinterpret_cast<float2*>(smem_raw);
-      float2* F = reinterpret_cast<float2*>(smem_raw + X_BYTES);
+      unsigned char* F = smem_raw + X_BYTES;
       float2* Y = reinterpret_cast<float2*>(smem_raw + X_BYTES + F_BYTES);
       const int lane = threadIdx.x;
       const int c = (int)cluster_ctarank();
@@ -169,9 +183,11 @@ struct ClusterConv {
          if constexpr(HAS_FILTER && FLT == Flt::SMEM) mbar_init(&fbar, 1);
          mbar_init(&xbar[0], 1);
          mbar_init(&xbar[1], 1);
+         if constexpr(BFP) mbar_init(&xbar[2], 1);
          fence_mbar_init();
          mbar_expect_tx(&xbar[0], XCHG_BYTES);
          mbar_expect_tx(&xbar[1], XCHG_BYTES);
+         if constexpr(BFP) mbar_expect_tx(&xbar[2], (uint32_t)((C - 1) * sizeof(float)));
       }
       __syncthreads();
       cluster_arrive_relaxed();
@@ -179,20 +195,25 @@ struct ClusterConv {
       // ---- this CTA's filter block (row c of the chain order), TMA bulk prefetch
       if constexpr(HAS_FILTER && FLT == Flt::SMEM) {
          if(lane == 0) {
-            mbar_expect_tx(&fbar, (uint32_t)(B * 8));
-            bulk_g2s(F, static_cast<const float2*>(args.b) + (size_t)(tr * args.filter_stride) + (size_t)c * B,
-                     (uint32_t)(B * 8), &fbar);
+            mbar_expect_tx(&fbar, (uint32_t)(B * FELEM));
+            bulk_g2s(F, static_cast<const unsigned char*>(args.b) +
+                            ((size_t)(tr * args.filter_stride) + (size_t)c * B) * FELEM,
+                     (uint32_t)(B * FELEM), &fbar);
          }
       }
 
       // ---- 1. outer DIF pass on this CTA's columns, taps straight from HBM
       float2 x[R];
+      float sa = 1.0f;
+      if constexpr(BFP) sa = __ldg(args.a_scale + tr);
 #pragma unroll
       for(int s = 0; s < G; ++s)
 #pragma unroll
-         for(int q = 0; q < C; ++q)
-            x[s * C + q] = ld_stream(static_cast<const float2*>(args.a) + gbase + (size_t)q * B + c * CB + lane +
-                                     T * s);
+         for(int q = 0; q < C; ++q) {
+            const size_t gi = gbase + (size_t)q * B + c * CB + lane + T * s;
+            if constexpr(BFP) x[s * C + q] = bfp_dequant(ld_stream(static_cast<const uint32_t*>(args.a) + gi), sa);
+            else x[s * C + q] = ld_stream(static_cast<const float2*>(args.a) + gi);
+         }
       outer<-1>(x, c, lane, args.tw);
       cluster_wait();   // every CTA of the cluster runs, its mbarriers armed
 
@@ -224,13 +245,29 @@ struct ClusterConv {
       fwd_all(X, x, lane, args.tw, std::make_integer_sequence<int, I::NP>{});
       if constexpr(HAS_FILTER) {
          float2 f[R];
+         float sb = 1.0f;
+         if constexpr(BFP) sb = __ldg(args.b_scale + (args.filter_stride ? tr : 0));
+         const size_t fbase = (size_t)(tr * args.filter_stride) + (size_t)c * B;
          if constexpr(FLT == Flt::SMEM) {
             mbar_wait(&fbar, 0, args.status);
 #pragma unroll
-            for(int k = 0; k < R; ++k) f[k] = F[lane + k * T];
+            for(int k = 0; k < R; ++k) {
+               if constexpr(BFP) f[k] = bfp_dequant(reinterpret_cast<const uint32_t*>(F)[lane + k * T], sb);
+               else f[k] = reinterpret_cast<const float2*>(F)[lane + k * T];
+            }
+         } else if constexpr(BFP) {
+            const uint4* fp = reinterpret_cast<const uint4*>(static_cast<const uint32_t*>(args.b) + fbase +
+                                                             (size_t)lane * R);
+#pragma unroll
+            for(int k = 0; k < R; k += 4) {
+               const uint4 w = __ldg(fp + k / 4);
+               f[k] = bfp_dequant(w.x, sb);
+               f[k + 1] = bfp_dequant(w.y, sb);
+               f[k + 2] = bfp_dequant(w.z, sb);
+               f[k + 3] = bfp_dequant(w.w, sb);
+            }
          } else {
-            const float4* fp = reinterpret_cast<const float4*>(static_cast<const float2*>(args.b) +
-                                                               (size_t)(tr * args.filter_stride) + (size_t)c * B +
+            const float4* fp = reinterpret_cast<const float4*>(static_cast<const float2*>(args.b) + fbase +
                                                                (size_t)lane * R);
 #pragma unroll
             for(int k = 0; k < R; k += 2) {
@@ -269,20 +306,55 @@ struct ClusterConv {
 #pragma unroll
          for(int q = 0; q < C; ++q) x[s * C + q] = Y[q * CB + lane + T * s];
       outer<+1>(x, c, lane, args.tw);
+      if constexpr(BFP) {
+         // ---- 6. abs-max of the whole transform: this CTA's share, then one
+         // 4-byte st.async to every peer; quantise with the cluster maximum
+         float m = 0.0f;
 #pragma unroll
-      for(int s = 0; s < G; ++s)
+         for(int i = 0; i < R; ++i) m = fmaxf(m, fmaxf(fabsf(x[i].x), fabsf(x[i].y)));
 #pragma unroll
-         for(int q = 0; q < C; ++q)
-            st_stream(static_cast<float2*>(args.out) + gbase + (size_t)q * B + c * CB + lane + T * s,
-                      x[s * C + q]);
+         for(int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+         if((lane & 31) == 0) wmax[lane >> 5] = m;
+         __syncthreads();
+         if(lane == 0) {
+#pragma unroll
+            for(int w = 1; w < T / 32; ++w) m = fmaxf(m, wmax[w]);
+            const uint32_t cb = smem_u32(&cmax[c]), mb = smem_u32(&xbar[2]);
+            cmax[c] = m;
+#pragma unroll
+            for(int q = 0; q < C; ++q)
+               if(q != c) st_async(map_remote(cb, q), m, map_remote(mb, q));
+         }
+         mbar_wait<true>(&xbar[2], 0, args.status);
+         __syncthreads();
+         m = 0.0f;
+#pragma unroll
+         for(int q = 0; q < C; ++q) m = fmaxf(m, cmax[q]);
+         const float mx = fmaxf(m, 1e-30f);
+         const float inv = 32767.0f / mx;
+         uint32_t* o = static_cast<uint32_t*>(args.out);
+#pragma unroll
+         for(int s = 0; s < G; ++s)
+#pragma unroll
+            for(int q = 0; q < C; ++q)
+               st_stream(o + gbase + (size_t)q * B + c * CB + lane + T * s, bfp_quant(x[s * C + q], inv));
+         if(c == 0 && lane == 0) args.out_scale[tr] = mx / 32767.0f;
+      } else {
+#pragma unroll
+         for(int s = 0; s < G; ++s)
+#pragma unroll
+            for(int q = 0; q < C; ++q)
+               st_stream(static_cast<float2*>(args.out) + gbase + (size_t)q * B + c * CB + lane + T * s,
+                         x[s * C + q]);
+      }
    }
 };
 
-template<class Inner, int C, int OUT_L, int OUT_SHIFT, Mid MID, Flt FLT>
+template<class Inner, int C, int OUT_L, int OUT_SHIFT, Mid MID, Flt FLT, bool BFP>
 __global__ void __launch_bounds__(Inner::T, min_blocks<Inner::T>())
 conv_cluster_kernel(const ConvArgs args)
 {
-   ClusterConv<Inner, C, OUT_L, OUT_SHIFT, MID, FLT>::run(args);
+   ClusterConv<Inner, C, OUT_L, OUT_SHIFT, MID, FLT, BFP>::run(args);
 }
 
 }  // namespace fufft

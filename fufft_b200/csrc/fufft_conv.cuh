@@ -481,18 +481,25 @@ struct ConvKernel {
    }
 };
 
-// occupancy target: FUFFT_RESIDENT_THREADS per SM (512 = two 256-thread CTAs,
-// which leaves ptxas 128 registers per thread: no spills in any variant)
+// occupancy target in resident threads per SM.  fp32: 512 (two 256-thread
+// CTAs, up to 128 registers per thread, no spills).  int16-BFP: 1024 (64
+// registers): the BFP kernel moves half the bytes and is bound by issue and
+// latency, and four CTAs per SM measured 10-20% faster at N = 512..4096;
+// fp32 measured 3-9% slower at 768 or 1024.
 #ifndef FUFFT_RESIDENT_THREADS
 #define FUFFT_RESIDENT_THREADS 512
 #endif
-template<int THREADS> constexpr int min_blocks()
+#ifndef FUFFT_RESIDENT_THREADS_BFP
+#define FUFFT_RESIDENT_THREADS_BFP 1024
+#endif
+template<int THREADS, int RESIDENT = FUFFT_RESIDENT_THREADS> constexpr int min_blocks()
 {
-   return THREADS >= FUFFT_RESIDENT_THREADS ? 1 : FUFFT_RESIDENT_THREADS / THREADS;
+   return THREADS >= RESIDENT ? 1 : RESIDENT / THREADS;
 }
 
 template<class C, int CPB, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>
-__global__ void __launch_bounds__(CPB * C::T, min_blocks<CPB * C::T>())
+__global__ void __launch_bounds__(CPB * C::T, min_blocks<CPB * C::T, IN == In::BFP ? FUFFT_RESIDENT_THREADS_BFP
+                                                                                  : FUFFT_RESIDENT_THREADS>())
 conv_kernel(const ConvArgs args)
 {
    ConvKernel<C, CPB, IN, OUT, MID, FLT, FBFP>::run(args);

@@ -264,6 +264,8 @@ bool conv2d_supported_r16(int h, int w);
 fufft_status cluster_conv1d(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev);
 fufft_status cluster_large(int r_out, int mid_n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st,
                            int dev);
+fufft_status cluster_large_bfp(int r_out, int mid_n, fufft_midop mid, bool bperm, const ConvArgs& a,
+                               cudaStream_t st, int dev);
 fufft_status cluster_conv2d(int h, int w, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev);
 bool cluster_conv2d_shape(int h, int w);
 constexpr int MAX_N_CLUSTER = 65536;   // radix-16 layouts, one cluster-fused kernel

@@ -254,6 +254,25 @@ fufft_status fufft_conv_large_bfp(const int16_t* aq, const float* a_scale, const
    DeviceCtx c;
    if((s = device_ctx(&c)) != FUFFT_OK) return s;
    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+   if(lout == 1 && layout_radix(layout) == 16) {
+      // one outer level: the whole BFP four-step in one cluster kernel, 12 B
+      // per point of HBM traffic and no use of the workspace (each CTA reads
+      // the positions it later writes, so oq may alias aq); multi-kernel form
+      // below if the device cannot host the cluster
+      ConvArgs ca{};
+      ca.tw = c.tw;
+      ca.status = c.status;
+      ca.batch = batch;
+      ca.a = aq;
+      ca.a_scale = a_scale;
+      ca.b = bq;
+      ca.b_scale = b_scale;
+      ca.out = oq;
+      ca.out_scale = o_scale;
+      ca.filter_stride = n;
+      s = cluster_large_bfp(r_out, mid, midop, layout_bperm(layout), ca, st, c.device);
+      if(s != FUFFT_ERR_UNSUPPORTED) return s;
+   }
    float2* ws = static_cast<float2*>(workspace);
    OuterArgs oa{};
    oa.n = n;

@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 import torch
 
-from oracle.oracle import MID_NONE, rel_l2
+from oracle.oracle import MID_CONJ, MID_MULTIPLY, MID_NONE, rel_l2
 
 pytestmark = pytest.mark.gpu
 F32_TOL = 2e-6
@@ -80,6 +80,60 @@ def test_large_bfp(ops, oracle, n, batch):
     # whole pipeline against the unquantised fp64 convolution
     rel = rel_l2(got[:n], oracle.conv_f64(a[:n], spec[:n], n))
     assert rel < 3e-4
+
+
+@pytest.mark.parametrize("r_out,mid", [(16, 2048), (8, 4096)])
+@pytest.mark.parametrize("lname", ["R16", "R16_BPERM"])
+@pytest.mark.parametrize("midop", [MID_MULTIPLY, MID_CONJ, MID_NONE])
+def test_large_bfp_cluster(ops, oracle, r_out, mid, lname, midop):
+    """N=32768 with one outer level: the BFP four-step runs as one cluster
+    kernel (int16 in, filter and out; cluster-wide abs-max for the scale)"""
+    import ctypes as ct
+    from fufft_b200._lib import lib
+    n, batch = 32768, 3
+    layout = getattr(ops, "LAYOUT_" + lname)
+    rng = np.random.default_rng(n + r_out + midop)
+    a = (rng.standard_normal(n * batch) + 1j * rng.standard_normal(n * batch)).astype(np.complex64)
+    taps = (rng.uniform(-1, 1, n * batch) + 1j * rng.uniform(-1, 1, n * batch))
+    spec = (np.fft.fft(taps.reshape(batch, n), axis=1) / n).astype(np.complex64)
+    rev = oracle.rev_table(oracle.foursteps_chain(n, r_out, mid, 16), n)
+    b_dr = np.ascontiguousarray(spec[:, rev]).ravel()
+    aq, as_ = oracle.bfp_quantize(a, n)
+    bq, bs = oracle.bfp_quantize(b_dr, n)
+    # register-boundary layout: the int16 pairs of each mid-point chunk in bperm order
+    bk = bq if lname == "R16" else _chunk_bperm(bq.view(np.int32).ravel(), mid, 16).view(np.int16).reshape(-1, 2)
+    oq, os_ = ops.conv_large_bfp(_dev(aq), _dev(as_), _dev(bk), _dev(bs), n, layout, midop, r_out=r_out,
+                                 mid_size=mid)
+    got = oracle.bfp_dequantize(oq.cpu().numpy(), os_.cpu().numpy(), n)
+    ad = oracle.bfp_dequantize(aq, as_, n).astype(np.complex128).reshape(batch, n)
+    bd = oracle.bfp_dequantize(bq, bs, n).astype(np.complex128).reshape(batch, n)
+    bnat = np.empty_like(bd)
+    bnat[:, rev] = bd
+    A = np.fft.fft(ad, axis=1)
+    if midop == MID_MULTIPLY:
+        want_f = oracle.conv_foursteps(oracle.bfp_dequantize(aq, as_, n), oracle.bfp_dequantize(bq, bs, n),
+                                       n, r_out, mid, 16)
+        wq, ws = oracle.bfp_quantize(want_f, n)
+        assert rel_l2(got, oracle.bfp_dequantize(wq, ws, n)) <= BFP_TOL
+        ref = np.fft.ifft(A * bnat, axis=1) * n
+    elif midop == MID_CONJ:
+        ref = np.fft.ifft(A * np.conj(bnat), axis=1) * n
+    else:
+        ref = ad * n
+    assert rel_l2(got, ref.ravel()) < 1e-4
+    # in place: the result may overwrite the signal
+    if midop == MID_MULTIPLY:
+        buf = _dev(aq)
+        os2 = torch.empty(batch, dtype=torch.float32, device="cuda")
+        ws_ = torch.empty(int(lib().fufft_conv_large_bfp_workspace(n, batch)), dtype=torch.uint8, device="cuda")
+        bkd, asd, bsd = _dev(bk), _dev(as_), _dev(bs)
+        rc = lib().fufft_conv_large_bfp(buf.data_ptr(), asd.data_ptr(), bkd.data_ptr(), bsd.data_ptr(),
+                                        buf.data_ptr(), os2.data_ptr(), n, batch, r_out, mid, layout, midop,
+                                        ws_.data_ptr(), ws_.numel(), None)
+        assert rc == 0
+        assert torch.equal(buf.cpu(), oq.cpu()) and torch.equal(os2.cpu(), os_.cpu())
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
 
 
 def test_large_full_size_properties(ops):
