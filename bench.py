@@ -272,8 +272,8 @@ def run_ncu_case(which: str = "headline"):
     """one launch of each kernel of a group, on a batch of a few hundred MB
     (> L2), for ncu.  headline: fp32 (register-boundary filter), fp32 (linear
     chain filter), int16-BFP (linear chain filter) at N=4096; cluster: the
-    cluster-fused N=32768 (radix-16 chain and the four-step recipe) and 2-D
-    256x256"""
+    cluster-fused N=32768 (radix-16 chain and the four-step recipe), 2-D
+    256x256 and the int16-BFP four-step N=32768"""
     import torch
     from fufft_b200 import ops
     ops.init()
@@ -287,6 +287,9 @@ def run_ncu_case(which: str = "headline"):
         ops.conv(a, b, n, ops.LAYOUT_R16_BPERM, out=o)
         ops.conv_large(o, b, n, ops.LAYOUT_R16_BPERM, r_out=16, mid_size=2048)
         ops.conv2d(a, b[:65536], 256, 256, ops.LAYOUT_R16_BPERM, filter_stride=0, out=o)
+        aq, as_ = ops.bfp_pack(a, n)
+        bq, bs = ops.bfp_pack(b, n)
+        ops.conv_large_bfp(aq, as_, bq, bs, n, ops.LAYOUT_R16_BPERM, r_out=16, mid_size=2048)
         torch.cuda.synchronize()
         assert ops.device_status() == 0
         return
