@@ -42,6 +42,15 @@ def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
+def _hptr(t: torch.Tensor | None):
+    """address of a contiguous HOST tensor"""
+    if t is None:
+        return None
+    if t.is_cuda or not t.is_contiguous():
+        raise ValueError("expected a contiguous host tensor")
+    return t.data_ptr()
+
+
 def _ptr(t: torch.Tensor | None):
     if t is None:
         return None
@@ -150,6 +159,33 @@ def conv2d(a: torch.Tensor, b: torch.Tensor | None, h: int, w: int, layout: int 
     fs = h * w if filter_stride is None else filter_stride
     check(lib().fufft_conv2d_f32(_ptr(a), _ptr(bt), _ptr(out), h, w, _batch(a, h * w), layout, mid, fs, _stream()),
           "fufft_conv2d_f32")
+    return out
+
+
+def conv_host_workspace(n: int, batch: int, filter_stride: int, device=None) -> torch.Tensor:
+    """device workspace for conv_host (allocate once, reuse across calls)"""
+    need = int(lib().fufft_conv_host_workspace(n, batch, filter_stride))
+    return torch.empty(max(need, 1), dtype=torch.uint8, device=device or "cuda")
+
+
+def conv_host(a: torch.Tensor, b: torch.Tensor | None, out: torch.Tensor, n: int, layout: int = LAYOUT_R16_BPERM,
+              mid: int = MID_MULTIPLY, filter_stride: int | None = None,
+              workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """fused convolution of HOST tensors (pinned for overlap): chunked upload /
+    convolve / download pipeline on the current device, asynchronous on the
+    current stream"""
+    a, out = _complex(a), _complex(out)
+    if a.is_cuda or out.is_cuda or (b is not None and b.is_cuda):
+        raise ValueError("conv_host takes host tensors")
+    bt = None if b is None else _complex(b)
+    batch = _batch(a, n)
+    if out.numel() < a.numel():
+        raise ValueError("out is smaller than a")
+    fs = (n if bt is None or bt.numel() > n else 0) if filter_stride is None else filter_stride
+    if workspace is None:
+        workspace = conv_host_workspace(n, batch, fs)
+    check(lib().fufft_conv_c2c_f32_host(_hptr(a), _hptr(bt), _hptr(out), n, batch, layout, mid, fs, _ptr(workspace),
+                                        workspace.numel(), _stream()), "fufft_conv_c2c_f32_host")
     return out
 
 

@@ -36,6 +36,7 @@
 extern "C" {
 #endif
 
+#include <stddef.h>
 #include <stdint.h>
 
 typedef struct CUstream_st* fufft_stream_t; /* same type as cudaStream_t */
@@ -133,6 +134,21 @@ fufft_status fufft_filter_permute2d(const float* spec_natural, float* out, int h
 fufft_status fufft_conv_c2c_f32(const float* a, const float* b, float* out, int n, int64_t batch,
                                 fufft_layout layout, fufft_midop mid, int64_t filter_stride,
                                 fufft_stream_t stream);
+
+/* ---- fused fp32 convolution of HOST data --------------------------------
+ * The same convolution for a, b, out in host memory (pinned for overlap):
+ * the batch goes through the device in ~32 MiB chunks, uploads, kernels and
+ * downloads of consecutive chunks overlapping on private streams; ordered
+ * after the work queued on `stream`, and `stream` waits for its end.
+ * filter_stride must be n or 0.  `workspace` is device memory of at least
+ * fufft_conv_host_workspace(n, batch, filter_stride) bytes, 256-byte
+ * aligned, not used by anything else until the call's work has finished.
+ * No reference counterpart: the reference's caller copies the batch in and
+ * out around the launches (bench_fufft.cu:183-186, :227). */
+size_t fufft_conv_host_workspace(int n, int64_t batch, int64_t filter_stride);
+fufft_status fufft_conv_c2c_f32_host(const float* a, const float* b, float* out, int n, int64_t batch,
+                                     fufft_layout layout, fufft_midop mid, int64_t filter_stride, void* workspace,
+                                     size_t workspace_bytes, fufft_stream_t stream);
 
 /* ---- fused 2-D convolution ----------------------------------------------
  * Row-major h x w images: 2-D DFT (columns then rows), mid-op against the

@@ -222,3 +222,34 @@ def test_errors_and_status(ops):
     ops.conv(empty, empty, 1024, ops.LAYOUT_R16)       # batch 0: nothing to do
     torch.cuda.synchronize()
     assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("n,batch,fs", [(4096, 37, "per"), (1024, 9000, "per"), (512, 30000, "shared"),
+                                        (32768, 5, "per")])
+def test_conv_host_pipeline(ops, oracle, n, batch, fs):
+    """fufft_conv_c2c_f32_host: host buffers through the chunked upload /
+    convolve / download pipeline equal the device-resident call bit for bit,
+    over several chunks and a ragged last chunk; a shared filter is uploaded once"""
+    rng = np.random.default_rng(n + batch)
+    a = (rng.standard_normal(batch * n) + 1j * rng.standard_normal(batch * n)).astype(np.complex64)
+    nb = batch if fs == "per" else 1
+    b = ((rng.uniform(-1, 1, nb * n) + 1j * rng.uniform(-1, 1, nb * n)) / n).astype(np.complex64)
+    stride = n if fs == "per" else 0
+    want = _host(ops.conv(_dev(a), _dev(b), n, ops.LAYOUT_R16_BPERM, MID_MULTIPLY, filter_stride=stride))
+    ha = torch.from_numpy(a).pin_memory()
+    hb = torch.from_numpy(b).pin_memory()
+    ho = torch.empty_like(ha).pin_memory()
+    ws = ops.conv_host_workspace(n, batch, stride)
+    for _ in range(2):       # the workspace is reused by consecutive calls on one stream
+        ho.zero_()
+        ops.conv_host(ha, hb, ho, n, ops.LAYOUT_R16_BPERM, MID_MULTIPLY, filter_stride=stride, workspace=ws)
+        torch.cuda.current_stream().synchronize()
+        assert np.array_equal(ho.numpy(), want)
+    # mid-op none needs no filter
+    ho.zero_()
+    ops.conv_host(ha, None, ho, n, ops.LAYOUT_R16_BPERM, MID_NONE, workspace=ws)
+    torch.cuda.current_stream().synchronize()
+    assert rel_l2(ho.numpy() / n, a) <= F32_TOL
+    from fufft_b200._lib import FufftError
+    with pytest.raises(FufftError):      # too small a workspace
+        ops.conv_host(ha, hb, ho, n, ops.LAYOUT_R16_BPERM, MID_MULTIPLY, filter_stride=stride, workspace=ws[:64])
