@@ -39,6 +39,8 @@ SIGNATURES = {
     "fufft_fwd_f32": (_I, [_P, _P, _I, _I64, _I, _P]),
     "fufft_apply_f32": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I64, _I64, _P]),
     "fufft_fwd_r2_f32": (_I, [_P, _P, _P, _I, _I64, _I, _P]),
+    "fufft_c2c_f32": (_I, [_P, _P, _I, _I64, _I, _P]),
+    "fufft_filter_from_taps_f32": (_I, [_P, _P, _I, _I64, _I, _P]),
     "fufft_conv_host_workspace": (ct.c_size_t, [_I, _I64, _I64]),
     "fufft_conv_c2c_f32_host": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I64, _P, ct.c_size_t, _P]),
     "fufft_apply_grid_f32": (_I, [_P, _I64, _P, _I64, _P, _I, _I, _I, _P]),

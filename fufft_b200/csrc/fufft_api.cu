@@ -122,6 +122,42 @@ fufft_status fufft_apply_f32(const float* spec, const float* b, float* out, int 
    return (R == 8 ? family_apply_r8 : family_apply_r16)(n, mid, layout_bperm(layout), args, st, dev);
 }
 
+fufft_status fufft_filter_from_taps_f32(const float* taps, float* out, int n, int64_t batch, fufft_layout layout,
+                                       fufft_stream_t stream)
+{
+   ConvArgs args{};
+   int R = 0, dev = 0;
+   bool skip;
+   fufft_status s = prepare(n, batch, layout, &R, &args, &dev, &skip);
+   if(s != FUFFT_OK || skip) return s;
+   if(!taps || !out) return FUFFT_ERR_INVALID_ARG;
+   if(!aligned(taps, 8) || !aligned(out, 16)) return FUFFT_ERR_MISALIGNED;
+   args.a = taps;
+   args.out = out;
+   args.spec_scale = 1.0f / (float)n;
+   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+   return (R == 8 ? family_fwd_r8 : family_fwd_r16)(n, FUFFT_MID_NONE, layout_bperm(layout), args, st, dev);
+}
+
+fufft_status fufft_c2c_f32(const float* in, float* out, int n, int64_t batch, int sign, fufft_stream_t stream)
+{
+   if(sign != -1 && sign != 1) return FUFFT_ERR_INVALID_ARG;
+   ConvArgs args{};
+   int R = 0, dev = 0;
+   bool skip;
+   // radix-16 chain from 16 points on, radix 8 for n = 8
+   const fufft_layout layout = n >= 16 ? FUFFT_LAYOUT_R16 : FUFFT_LAYOUT_R8;
+   fufft_status s = prepare(n, batch, layout, &R, &args, &dev, &skip);
+   if(s != FUFFT_OK || skip) return s;
+   if(!in || !out) return FUFFT_ERR_INVALID_ARG;
+   if(!aligned(in, 8) || !aligned(out, 8)) return FUFFT_ERR_MISALIGNED;
+   args.a = in;
+   args.out = out;
+   args.conj_io = sign > 0;
+   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+   return (R == 8 ? family_c2c_r8 : family_c2c_r16)(n, FUFFT_MID_NONE, false, args, st, dev);
+}
+
 fufft_status fufft_fwd_r2_f32(const float* xr, const float* yr, float* spec, int n, int64_t batch,
                               fufft_layout layout, fufft_stream_t stream)
 {

@@ -34,8 +34,9 @@ namespace fufft {
 // chain order (thread `lane` owns the R consecutive positions R*lane ..);
 // SPEC_BP: the same spectrum in register-boundary order, position R*lane + k
 // stored at lane + k*T (the bperm filter map) -- coalesced for every warp access
+// Out::NAT: the spectrum in natural order (plain c2c transform, no inverse).
 enum class In { C32, BFP, REAL2, SPEC, SPEC_BP };
-enum class Out { C32, BFP, REAL2, SPEC, SPEC_BP };
+enum class Out { C32, BFP, REAL2, SPEC, SPEC_BP, NAT };
 enum class Mid { NONE, MUL, CONJ };        // pointwise operation between the transforms
 enum class Flt { NONE, SMEM, GLOBAL };     // filter read: TMA-staged register-boundary
                                            // layout, or chain order straight from HBM
@@ -97,6 +98,8 @@ struct ConvArgs {
    long long spec_stride;    // SPEC input: elements between consecutive transforms' spectra
    long long scale_div;      // BFP filter scale of transform t: b_scale[t / scale_div] (0, 1: per transform)
    long long grid_filters;   // SPEC input, > 0: transform t = s * grid_filters + f applies filter f to spectrum s
+   int conj_io;              // Out::NAT: conjugate on load and store (the inverse transform)
+   float spec_scale;         // spectrum outputs: multiply by this when nonzero (filter preparation: 1/n)
    long long batch;
    const float2* tw;         // the device's twiddle tables (tw_offset layout)
    unsigned int* status;     // device status word (bounded-wait reports)
@@ -227,6 +230,22 @@ __device__ __forceinline__ uint32_t bfp_quant(float2 v, float inv)
    return r;
 }
 
+// natural (frequency) index of chain position p of a 1-D chain: the digits
+// of p, one per pass (pass 0 most significant), written back in reverse order
+template<class C>
+__device__ __forceinline__ int chain_natural(int p)
+{
+   int out = 0, pos = ilog2c(C::N), op = 0;
+#pragma unroll
+   for(int k = 0; k < C::NP; ++k) {
+      const int w = ilog2c(C::radix(k));
+      pos -= w;
+      out |= ((p >> pos) & ((1 << w) - 1)) << op;
+      op += w;
+   }
+   return out;
+}
+
 template<class C_, int CPB, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>
 struct ConvKernel {
    using C = C_;
@@ -346,7 +365,11 @@ struct ConvKernel {
                const size_t gi = gbase + lane + (size_t)T * (s + G0 * k);
                float2 v = make_float2(0.f, 0.f);
                if(active) {
-                  if constexpr(IN == In::C32) v = ld_stream(static_cast<const float2*>(args.a) + gi);
+                  if constexpr(IN == In::C32) {
+                     v = ld_stream(static_cast<const float2*>(args.a) + gi);
+                     if constexpr(OUT == Out::NAT)
+                        if(args.conj_io) v.y = -v.y;
+                  }
                   else if constexpr(IN == In::BFP)
                      v = bfp_dequant(ld_stream(static_cast<const uint32_t*>(args.a) + gi), sa);
                   else v = make_float2(ld_stream(static_cast<const float*>(args.a) + gi),
@@ -376,7 +399,28 @@ struct ConvKernel {
       }
 
       // ---- register boundary: x[k] is the spectrum at chain position R*lane + k
-      if constexpr(SPEC_OUT) {
+      if constexpr(OUT == Out::NAT) {
+         // natural order: scatter through the exchange buffer, store coalesced
+         static_assert(C::NPC == 0, "natural-order output of 1-D chains");
+         sched_fence();
+         slot_sync<T, CPB>(slot);   // every thread is past its last read of X
+#pragma unroll
+         for(int k = 0; k < R; ++k) X[SwzEngine::map(off + chain_natural<C>(R * lane + k))] = x[k];
+         slot_sync<T, CPB>(slot);
+         if(active) {
+            const float sgn = args.conj_io ? -1.0f : 1.0f;
+#pragma unroll
+            for(int u = 0; u < R; ++u) {
+               const float2 v = X[SwzEngine::map(off + lane + T * u)];
+               st_stream(static_cast<float2*>(args.out) + gbase + lane + T * u, make_float2(v.x, sgn * v.y));
+            }
+         }
+         return;
+      } else if constexpr(SPEC_OUT) {
+         if(args.spec_scale != 0.0f) {
+#pragma unroll
+            for(int k = 0; k < R; ++k) x[k] = make_float2(x[k].x * args.spec_scale, x[k].y * args.spec_scale);
+         }
          if(active) {
             if constexpr(OUT == Out::SPEC_BP) {
                float2* sp = static_cast<float2*>(args.out) + gbase;

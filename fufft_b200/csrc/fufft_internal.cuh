@@ -248,6 +248,8 @@ fufft_status family_apply_r2_r8(int, fufft_midop, bool, const ConvArgs&, cudaStr
 fufft_status family_apply_r2_r16(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
 fufft_status family_fwd_r2_r8(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
 fufft_status family_fwd_r2_r16(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
+fufft_status family_c2c_r8(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
+fufft_status family_c2c_r16(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
 fufft_status family_r2_r8(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
 fufft_status family_r2_r16(int, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);
 fufft_status family_conv2d_r8(int h, int w, fufft_midop, bool, const ConvArgs&, cudaStream_t, int);

@@ -189,6 +189,23 @@ def conv_host(a: torch.Tensor, b: torch.Tensor | None, out: torch.Tensor, n: int
     return out
 
 
+def filter_from_taps(taps: torch.Tensor, n: int, layout: int = LAYOUT_R16_BPERM) -> torch.Tensor:
+    """complex filter taps (natural order) -> filter spectrum x 1/n in `layout`, on the device"""
+    taps = _complex(taps)
+    out = torch.empty_like(taps)
+    check(lib().fufft_filter_from_taps_f32(_ptr(taps), _ptr(out), n, _batch(taps, n), layout, _stream()),
+          "fufft_filter_from_taps_f32")
+    return out
+
+
+def c2c(a: torch.Tensor, n: int, sign: int = -1, out: torch.Tensor | None = None) -> torch.Tensor:
+    """natural-order DFT of each n-point transform (sign -1), or the unnormalised inverse (+1)"""
+    a = _complex(a)
+    out = torch.empty_like(a) if out is None else _complex(out)
+    check(lib().fufft_c2c_f32(_ptr(a), _ptr(out), n, _batch(a, n), sign, _stream()), "fufft_c2c_f32")
+    return out
+
+
 def fwd(a: torch.Tensor, n: int, layout: int = LAYOUT_R8) -> torch.Tensor:
     a = _complex(a)
     spec = torch.empty_like(a)

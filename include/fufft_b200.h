@@ -115,6 +115,15 @@ fufft_status fufft_filter_permute_host(const float* spec_natural, float* out, in
 fufft_status fufft_filter_permute(const float* spec_natural, float* out, int n, int batch,
                                   fufft_layout layout, fufft_stream_t stream);
 
+/* Filter taps (natural order, complex, one row of n per filter) -> the
+ * filter spectrum with 1/n folded in, in `layout` (R8 / R16 / *_BPERM),
+ * one kernel on the device, n <= fufft_max_n for one CTA (4096 radix 8,
+ * 8192 radix 16).  Replaces the host-side preparation around the
+ * reference's kernels: spectrum of the taps, 1/n folded in
+ * (bench_fufft.cu:156-165), mixedrev permutation (bench_fufft.cu:166-170). */
+fufft_status fufft_filter_from_taps_f32(const float* taps, float* out, int n, int64_t batch, fufft_layout layout,
+                                       fufft_stream_t stream);
+
 /* 2-D: slot (r, c) of the chain order holds spectrum (rev_H(r), rev_W(c)),
  * each dimension reversed over its own chain ([lead, R, ...]; radix 8 on
  * power-of-8 sides reproduces the reference's rev8 map, verify_kernel.cpp:738-748);
@@ -178,6 +187,14 @@ fufft_status fufft_fwd_f32(const float* a, float* spec, int n, int64_t batch, fu
 fufft_status fufft_apply_f32(const float* spec, const float* b, float* out, int n, int64_t batch,
                              fufft_layout layout, fufft_midop mid, int64_t spec_stride,
                              int64_t filter_stride, fufft_stream_t stream);
+
+/* ---- natural-order transform -------------------------------------------
+ * out = DFT(in) (sign -1) or the unnormalised inverse (sign +1), natural
+ * order on both sides, 8 <= n <= 8192, in == out allowed.  Replaces the
+ * reference's forward-only fufft_c2c (fufft.cuh:878-904, radix-8 Stockham,
+ * powers of 8): one kernel, the DIF chain in registers and one swizzled
+ * shared-memory scatter into natural order. */
+fufft_status fufft_c2c_f32(const float* in, float* out, int n, int64_t batch, int sign, fufft_stream_t stream);
 
 /* ---- the one-signal-many-filters shape at scale (no reference counterpart:
  * the reference's apply pairs spectrum i with filter i, fufft.cuh:1393-1395)

@@ -333,6 +333,34 @@ int orc_fwd(int n, int radix, const cpx* a, cpx* spec, int batch)
    return 0;
 }
 
+/* natural-order c2c (the reference's Mode A fufft_c2c, fufft.cuh:878-904,
+ * forward only there; CPU transcription kernel_c2c, verify_kernel.cpp:1183-1201,
+ * a radix-8 Stockham chain for powers of 8).  Restated on this oracle's own
+ * DIF chain of the given radix, then the chain order undone with chain_rev:
+ * spec[chain_rev(p)] = dif[p].  sign = -1 forward; +1 the unnormalised
+ * inverse, computed as conj(forward(conj(x))). */
+int orc_c2c(int n, int radix, int sign, const cpx* in, cpx* out, int batch)
+{
+   int rad[32];
+   const int nrad = chain_of(n, radix, rad);
+   if(nrad < 0 || (sign != -1 && sign != 1)) return -1;
+   const size_t count = (size_t)n * batch;
+   cpx* tmp = (cpx*)malloc(count * sizeof(cpx));
+   if(!tmp) return -2;
+   for(size_t i = 0; i < count; i++) { tmp[i] = in[i]; if(sign > 0) tmp[i].im = -tmp[i].im; }
+   dif_chain(tmp, count, n, radix);
+   for(int p = 0; p < n; p++) {
+      const long long r = orc_chain_rev(p, rad, nrad);
+      for(int t = 0; t < batch; t++) {
+         cpx v = tmp[(size_t)t * n + p];
+         if(sign > 0) v.im = -v.im;
+         out[(size_t)t * n + r] = v;
+      }
+   }
+   free(tmp);
+   return 0;
+}
+
 /* split apply: spectrum (x) filter, then DIT.  kernel_pipeline_apply,
  * verify_kernel.cpp:815-836 (fufft.cuh:1375-1407; multiply only there, the
  * conjugate form is this library's addition) */

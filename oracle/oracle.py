@@ -63,6 +63,7 @@ class Oracle:
             "orc_bperm": (i, [_P, _P, i, i, i]),
             "orc_conv": (i, [i, i, i, _P, _P, _P, i, ll]),
             "orc_fwd": (i, [i, i, _P, _P, i]),
+            "orc_c2c": (i, [i, i, i, _P, _P, i]),
             "orc_apply": (i, [i, i, i, _P, _P, _P, i, ll]),
             "orc_conv_r2": (i, [i, i, _P, _P, _P, _P, _P, i, ll]),
             "orc_conv2d_pow8": (i, [i, i, _P, _P, _P, i, ll]),
@@ -132,6 +133,13 @@ class Oracle:
         a = _c64(a)
         out = np.empty_like(a)
         assert self.L.orc_fwd(n, radix, _ptr(a), _ptr(out), a.size // n) == 0
+        return out
+
+    def c2c(self, a, n: int, sign: int = -1, radix: int = 16) -> np.ndarray:
+        """natural-order transform (sign -1 forward, +1 unnormalised inverse)"""
+        a = _c64(a)
+        out = np.empty_like(a)
+        assert self.L.orc_c2c(n, radix, sign, _ptr(a), _ptr(out), a.size // n) == 0
         return out
 
     def apply(self, spec, b_dr, n: int, radix: int = 8, mid: int = MID_MULTIPLY,
@@ -325,6 +333,7 @@ class Reference:
             "ref_pipeline_v16f": (None, [i, i, _P, _P, _P, i]),
             "ref_pipeline_r16": (None, [i, i, _P, _P, _P, i]),
             "ref_pipeline_fwd": (None, [i, i, _P, _P, i]),
+            "ref_c2c": (None, [i, i, _P, _P, i]),
             "ref_pipeline_apply": (None, [i, i, _P, _P, _P, i]),
             "ref_conv_r2": (None, [i, i, _P, _P, _P, _P, _P, i]),
             "ref_conv2d": (None, [i, i, _P, _P, _P, i]),
@@ -367,6 +376,10 @@ class Reference:
 
     def pipeline_fwd(self, a, n, cpb=1):
         return self._run("ref_pipeline_fwd", n, cpb, a)
+
+    def c2c(self, a, n, cpb=1):
+        """the reference's natural-order forward c2c (kernel_c2c, N a power of 8)"""
+        return self._run("ref_c2c", n, cpb, a)
 
     def pipeline_apply(self, spec, b_dr, n, cpb=1):
         return self._run("ref_pipeline_apply", n, cpb, spec, b_dr)

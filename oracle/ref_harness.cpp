@@ -89,6 +89,16 @@ void ref_pipeline_r16(int N, int CPB, const float* a, const float* b16, float* o
    from_cf(o, out);
 }
 
+// natural-order forward c2c (Mode A, radix-8 Stockham; N a power of 8)
+void ref_c2c(int N, int CPB, const float* a, float* out, int batch)
+{
+   const int LOG8N = [](int n) { int s = 0; while(n > 1) { n /= 8; s++; } return s; }(N);
+   const size_t n = (size_t)N * batch;
+   std::vector<cf> o;
+   kernel_c2c(N, LOG8N, CPB, CPP_OPT, to_cf(a, n), o, batch);
+   from_cf(o, out);
+}
+
 void ref_pipeline_fwd(int N, int CPB, const float* a, float* spec, int batch)
 {
    int LEAD, NR8; factorise(N, LEAD, NR8);

@@ -253,3 +253,23 @@ def test_conv_host_pipeline(ops, oracle, n, batch, fs):
     from fufft_b200._lib import FufftError
     with pytest.raises(FufftError):      # too small a workspace
         ops.conv_host(ha, hb, ho, n, ops.LAYOUT_R16_BPERM, MID_MULTIPLY, filter_stride=stride, workspace=ws[:64])
+
+
+@pytest.mark.parametrize("lname", list(LAYOUTS))
+@pytest.mark.parametrize("n", [8, 64, 512, 4096, 8192])
+def test_filter_from_taps(ops, oracle, lname, n):
+    """taps -> spectrum x 1/n in the kernel layout on the device, against the
+    oracle's permutation of a float64 spectrum; then used by a convolution"""
+    layout, radix, v = LAYOUTS[lname]
+    if n < radix or n > ops.max_n(layout) or (n > 4096 and radix == 8):
+        pytest.skip("size outside the layout's one-kernel range")
+    batch = 3
+    rng = np.random.default_rng(n + layout)
+    taps = (rng.uniform(-1, 1, batch * n) + 1j * rng.uniform(-1, 1, batch * n)).astype(np.complex64)
+    spec = (np.fft.fft(taps.astype(np.complex128).reshape(batch, n), axis=1) / n).astype(np.complex64).ravel()
+    want = _filter(oracle, spec, n, radix, v)
+    got = _host(ops.filter_from_taps(_dev(taps), n, layout))
+    assert rel_l2(got, want) <= F32_TOL
+    a = (rng.standard_normal(batch * n) + 1j * rng.standard_normal(batch * n)).astype(np.complex64)
+    conv = _host(ops.conv(_dev(a), _dev(got), n, layout))
+    assert rel_l2(conv, oracle.conv_f64(a, spec, n)) <= 3e-6

@@ -144,3 +144,29 @@ def test_oracle_apply_grid_r2_is_real_conv(oracle, radix, mid):
             H = np.fft.fft(taps[f])
             ref = np.fft.ifft(X[i] * (np.conj(H) if mid == 2 else H)).real
             assert np.linalg.norm(got[i, f] - ref) / np.linalg.norm(ref) <= 2e-5
+
+
+@pytest.mark.parametrize("n", [8, 64, 512, 4096])
+def test_oracle_c2c_pinned_to_reference(oracle, n):
+    """natural-order c2c: the oracle's restatement (its own DIF chain +
+    chain_rev unscramble) against the reference's own kernel_c2c (radix-8
+    Stockham, verify_kernel.cpp:1183-1201) from oracle/_ref, on the
+    reference's seeded input (mt19937(N*131+CPB), verify_kernel.cpp:1277),
+    and against float64; the inverse undoes the forward"""
+    from oracle.oracle import Reference
+    try:
+        ref = Reference()
+    except OSError:
+        pytest.skip("oracle/_ref not built (the reference sources are absent)")
+    batch = 3
+    a, _ = oracle.gen_test(n, 1, batch)
+    want = ref.c2c(a, n)
+    for radix in (8, 16):
+        if n < radix:
+            continue
+        got = oracle.c2c(a, n, -1, radix)
+        assert rel_l2(got, want) <= 1e-6, radix
+        back = oracle.c2c(got, n, +1, radix) / n
+        assert rel_l2(back, a) <= 2e-6
+    f64 = np.fft.fft(a.astype(np.complex128).reshape(batch, n), axis=1).ravel()
+    assert rel_l2(want, f64) <= 2e-6
