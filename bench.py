@@ -421,6 +421,19 @@ def run_sweep(args):
                  f"(4 GiB out)", ms, nsig * nfilt * n, 4, 8 * n * (nsig // 2 + nfilt) + 16 * n * (nsig // 2),
                  points="real output points")
         del x, taps, b_nat, bp, xs, xr, yr, o
+    # 6: the rows beyond the configs -- natural-order c2c (16 B/pt: read + write)
+    # and filter preparation from taps, N=4096 over 1 GiB of signal
+    if 6 in cfgs:
+        n = 4096
+        batch = POINTS // n
+        a = torch.randn(batch * n, dtype=torch.complex64, device="cuda", generator=g)
+        o = torch.empty_like(a)
+        for sign, name in [(-1, "forward"), (1, "inverse")]:
+            ms = time_steps(torch, lambda: ops.c2c(a, n, sign, out=o), steps, warm, None)
+            emit(f"6: natural-order c2c {name} N={n} batch={batch}", ms, batch * n, 16)
+        ms = time_steps(torch, lambda: ops.filter_from_taps(a, n, ops.LAYOUT_R16_BPERM), steps, warm, None)
+        emit(f"6: filter from taps N={n} batch={batch} (R16_BPERM)", ms, batch * n, 16)
+        del a, o
     # config 4: 2-D 256x256 x 512 images, one shared filter
     if 4 in cfgs:
         h = w = 256
@@ -491,7 +504,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-case", nargs="?", const="headline", default=None, choices=["headline", "cluster"],
                     help="one launch per kernel of a group, for ncu")
-    ap.add_argument("--configs", default="1,2,3,4,5", help="sweep: which BASELINE.json configs (1-based)")
+    ap.add_argument("--configs", default="1,2,3,4,5,6",
+                    help="sweep: which BASELINE.json configs (1-based); 6 = c2c and filter preparation")
     ap.add_argument("--workload", choices=["batch", "dist", "sweep"], default="batch",
                     help="dist: one 2^26-point signal over all ranks (2, 4 or 8); sweep: every "
                          "BASELINE.json config on one GPU, one JSON line each")

@@ -128,3 +128,32 @@ def test_2d_exchanges_conflict_free(R, shapes):
             # has no such shapes).  Everything else is 1-way.
             lead_row_pass = R == 8 and p == len(passes2d(h, w, R)) - len(chain(w, R)) and r < R and M == 8
             assert worst_ways(addrs, width) <= (2 if lead_row_pass else 1), (R, h, w, p, r, M)
+
+
+def natural(p, n, R):
+    """chain position -> natural index (fufft_conv.cuh chain_natural)"""
+    out, pos, op = 0, n.bit_length() - 1, 0
+    for r in chain(n, R):
+        w = r.bit_length() - 1
+        pos -= w
+        out |= ((p >> pos) & ((1 << w) - 1)) << op
+        op += w
+    return out
+
+
+@pytest.mark.parametrize("n", [32, 64, 128, 256, 512, 1024, 2048, 4096, 8192])
+def test_natural_order_scatter(n):
+    """the c2c kernel's unscramble (Out::NAT, radix-16 chains): the scatter to
+    natural positions is at most 2-way, the coalesced read-back 1-way, and the
+    map is a permutation (the reference avoided this scatter for its 8-16-way
+    conflicts, fufft.cuh:920-924)"""
+    R = 16
+    T = n // R
+    assert sorted(natural(p, n, R) for p in range(n)) == list(range(n))
+    scat, rd = [], []
+    for tid in range(cpb(T) * T):
+        slot, lane = divmod(tid, T)
+        scat.append([swz(slot * n + natural(R * lane + k, n, R)) for k in range(R)])
+        rd.append([swz(slot * n + lane + T * u) for u in range(R)])
+    assert worst_ways(scat, 8) <= 2
+    assert worst_ways(rd, 8) == 1
