@@ -337,14 +337,19 @@ def run_dist(args, rank, world, dist):
 
 
 def time_flushed(torch, fn, steps, warmup, flush_bytes=512 << 20):
-    """per-step device time of fn with L2 flushed (a 512 MiB write) before every
-    step, outside the timed events; for workloads that fit in L2"""
+    """per-step device time of fn with L2 flushed before every step, outside
+    the timed events; for workloads that fit in L2.  The flush writes a
+    512 MiB buffer, then reads another 512 MiB one: the write evicts the
+    step's data, the read turns L2 into clean lines, so the timed step pays
+    neither for its own data in L2 nor for the write-back of the flush"""
     junk = torch.empty(flush_bytes, dtype=torch.uint8, device="cuda")
+    clean = torch.ones(flush_bytes // 4, dtype=torch.float32, device="cuda")
     for _ in range(warmup):
         fn()
     tot = 0.0
     for _ in range(steps):
         junk.fill_(1)
+        clean.sum()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         fn()

@@ -100,6 +100,7 @@ struct ConvArgs {
    long long grid_filters;   // SPEC input, > 0: transform t = s * grid_filters + f applies filter f to spectrum s
    int conj_io;              // Out::NAT: conjugate on load and store (the inverse transform)
    float spec_scale;         // spectrum outputs: multiply by this when nonzero (filter preparation: 1/n)
+   long long prefetch_ahead; // > 0: each CTA asks L2 for the data of the CTA this many blocks later
    long long batch;
    const float2* tw;         // the device's twiddle tables (tw_offset layout)
    unsigned int* status;     // device status word (bounded-wait reports)
@@ -333,6 +334,23 @@ struct ConvKernel {
          }
       }
 
+      // ---- L2 prefetch of the CTA that takes this slot one wave later: its
+      // signal and filter requests reach HBM while this CTA computes
+      if constexpr(IN == In::C32) {
+         if(threadIdx.x == 0 && args.prefetch_ahead > 0) {
+            const long long nt0 = tr0 + args.prefetch_ahead * CPB;
+            if(nt0 < args.batch) {
+               const long long left = args.batch - nt0;
+               const uint32_t cnt = (uint32_t)(left < CPB ? left : CPB);
+               prefetch_l2_bulk(static_cast<const float2*>(args.a) + (size_t)nt0 * N, cnt * N * 8);
+               if constexpr(HAS_FILTER)
+                  if(args.filter_stride == N)
+                     prefetch_l2_bulk(static_cast<const unsigned char*>(args.b) + (size_t)nt0 * N * FELEM,
+                                      cnt * N * FELEM);
+            }
+         }
+      }
+
       // ---- filter prefetch: one bulk copy per transform, completes on fbar
       if constexpr(HAS_FILTER && FLT == Flt::SMEM) {
          if(threadIdx.x == 0) {
@@ -541,9 +559,15 @@ template<int THREADS, int RESIDENT = FUFFT_RESIDENT_THREADS> constexpr int min_b
    return THREADS >= RESIDENT ? 1 : RESIDENT / THREADS;
 }
 
+// natural-order output (one transform direction, no filter): three CTAs per
+// SM, as the spectrum-output kernels reach on their own (~80 registers)
+template<In IN, Out OUT> constexpr int resident_threads()
+{
+   return IN == In::BFP ? FUFFT_RESIDENT_THREADS_BFP : OUT == Out::NAT ? 768 : FUFFT_RESIDENT_THREADS;
+}
+
 template<class C, int CPB, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>
-__global__ void __launch_bounds__(CPB * C::T, min_blocks<CPB * C::T, IN == In::BFP ? FUFFT_RESIDENT_THREADS_BFP
-                                                                                  : FUFFT_RESIDENT_THREADS>())
+__global__ void __launch_bounds__(CPB * C::T, min_blocks<CPB * C::T, resident_threads<IN, OUT>()>())
 conv_kernel(const ConvArgs args)
 {
    ConvKernel<C, CPB, IN, OUT, MID, FLT, FBFP>::run(args);

@@ -216,6 +216,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                 :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
+// hint: bring `bytes` of global memory into L2 (no destination, no
+// completion); src 16-byte aligned, bytes a multiple of 16
+__device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes)
+{
+   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(src), "r"(bytes) : "memory");
+}
 // 2-D tiled TMA load of box (x, y) of a tensor map into shared memory,
 // completion on `bar`.  Every CTA loads its own tiles from this GPU's memory.  x is
 // always 0 here (whole 128-byte rows), so the 16-byte rule on x holds.
