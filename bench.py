@@ -439,6 +439,23 @@ def run_sweep(args):
         ms = time_steps(torch, lambda: ops.filter_from_taps(a, n, ops.LAYOUT_R16_BPERM), steps, warm, None)
         emit(f"6: filter from taps N={n} batch={batch} (R16_BPERM)", ms, batch * n, 16)
         del a, o
+    # 7: the reference's own yardstick (its published ratios are against a
+    # cuFFT chain: README.md:12-13): cuFFT forward, pointwise multiply, cuFFT
+    # inverse (torch.fft, three launches), against the fused kernel, same data
+    if 7 in cfgs:
+        for n in (512, 1024, 2048, 4096):
+            batch = POINTS // n
+            a = torch.randn(batch, n, dtype=torch.complex64, device="cuda", generator=g)
+            b = torch.randn(batch, n, dtype=torch.complex64, device="cuda", generator=g) / n
+            bp = ops.filter_permute(b.view(-1), n, ops.LAYOUT_R16_BPERM)
+            o = torch.empty_like(a)
+            ms_cufft = time_steps(torch, lambda: torch.fft.ifft(torch.fft.fft(a, dim=1) * b, dim=1, norm="forward"),
+                                  steps, warm, None)
+            ms_fused = time_steps(torch, lambda: ops.conv(a.view(-1), bp, n, ops.LAYOUT_R16_BPERM, out=o.view(-1)),
+                                  steps, warm, None)
+            emit(f"7: cuFFT chain fp32 N={n} (fft, multiply, ifft; comparison only)", ms_cufft, batch * n, 24,
+                 fused_ms=round(ms_fused, 4), fused_speedup=round(ms_cufft / ms_fused, 2))
+            del a, b, bp, o
     # config 4: 2-D 256x256 x 512 images, one shared filter
     if 4 in cfgs:
         h = w = 256
@@ -509,8 +526,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-case", nargs="?", const="headline", default=None, choices=["headline", "cluster"],
                     help="one launch per kernel of a group, for ncu")
-    ap.add_argument("--configs", default="1,2,3,4,5,6",
-                    help="sweep: which BASELINE.json configs (1-based); 6 = c2c and filter preparation")
+    ap.add_argument("--configs", default="1,2,3,4,5,6,7",
+                    help="sweep: which BASELINE.json configs (1-based); 6 = c2c and filter preparation, "
+                         "7 = the cuFFT chain the reference compares against")
     ap.add_argument("--workload", choices=["batch", "dist", "sweep"], default="batch",
                     help="dist: one 2^26-point signal over all ranks (2, 4 or 8); sweep: every "
                          "BASELINE.json config on one GPU, one JSON line each")
