@@ -253,6 +253,10 @@ struct ConvKernel {
    static constexpr int N = C::N, R = C::R;
    static constexpr int T = C::T;
    static constexpr int THREADS = CPB * T;
+   // int16-BFP in and out: the transforms run on the raw mantissas and the
+   // product of the input and filter scales enters only the output scale
+   // (a convolution is linear), saving the multiplies of the dequantisation
+   static constexpr bool FOLD = IN == In::BFP && OUT == Out::BFP;
    static constexpr bool SPEC_IN = IN == In::SPEC || IN == In::SPEC_BP;
    static constexpr bool SPEC_OUT = OUT == Out::SPEC || OUT == Out::SPEC_BP;
    static constexpr bool HAS_FILTER = (MID != Mid::NONE) && !SPEC_OUT;
@@ -260,6 +264,13 @@ struct ConvKernel {
    static constexpr size_t X_BYTES = (size_t)CPB * N * sizeof(float2);
    static constexpr size_t F_BYTES = (HAS_FILTER && FLT == Flt::SMEM) ? (size_t)CPB * N * FELEM : 0;
    static constexpr size_t SMEM = X_BYTES + F_BYTES;
+
+   // BFP filter scale of transform t
+   __device__ __forceinline__ static float filter_scale(const ConvArgs& args, long long t, bool active)
+   {
+      return active ? __ldg(args.b_scale + (args.filter_stride ? (args.scale_div > 1 ? t / args.scale_div : t) : 0))
+                    : 0.0f;
+   }
 
    // element offset of transform t's filter.  Grid apply (one launch over every
    // spectrum x every filter): filter t % F; otherwise t * filter_stride.
@@ -375,7 +386,7 @@ struct ConvKernel {
          // ---- first DIF pass straight from HBM: x[s*r + k] = a[lane + T*(s + G*k)]
          constexpr int r0 = C::radix(0), G0 = R / r0;
          float sa = 1.0f;
-         if constexpr(IN == In::BFP) sa = active ? __ldg(args.a_scale + tr) : 0.0f;
+         if constexpr(IN == In::BFP && !FOLD) sa = active ? __ldg(args.a_scale + tr) : 0.0f;
 #pragma unroll
          for(int s = 0; s < G0; ++s)
 #pragma unroll
@@ -459,7 +470,7 @@ struct ConvKernel {
                mbar_wait(&fbar, 0, args.status);
                if constexpr(FBFP) {
                   const uint32_t* Fs = reinterpret_cast<const uint32_t*>(F) + off;
-                  const float sb = active ? __ldg(args.b_scale + (args.filter_stride ? (args.scale_div > 1 ? tr / args.scale_div : tr) : 0)) : 0.0f;
+                  const float sb = FOLD ? 1.0f : filter_scale(args, tr, active);
 #pragma unroll
                   for(int k = 0; k < R; ++k) f[k] = bfp_dequant(Fs[lane + k * T], sb);
                } else {
@@ -470,7 +481,7 @@ struct ConvKernel {
             } else {
                const size_t fbase = (size_t)filter_off(args, tr) + (size_t)lane * R;
                if constexpr(FBFP) {
-                  const float sb = active ? __ldg(args.b_scale + (args.filter_stride ? (args.scale_div > 1 ? tr / args.scale_div : tr) : 0)) : 0.0f;
+                  const float sb = FOLD ? 1.0f : filter_scale(args, tr, active);
                   const uint4* fp = reinterpret_cast<const uint4*>(static_cast<const uint32_t*>(args.b) + fbase);
 #pragma unroll
                   for(int k = 0; k < R; k += 4) {
@@ -514,8 +525,11 @@ struct ConvKernel {
 #pragma unroll
                for(int o = T / 2; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
             }
-            const float mx = fmaxf(m, 1e-30f);
-            const float inv = 32767.0f / mx;
+            // m is the abs-max of the raw result; the true one is m * fold
+            float fold = active ? __ldg(args.a_scale + tr) : 0.0f;
+            if constexpr(HAS_FILTER && FBFP) fold *= filter_scale(args, tr, active);
+            const float mx = fmaxf(m * fold, 1e-30f);
+            const float inv = (32767.0f / mx) * fold;
             if(active) {
                uint32_t* o = static_cast<uint32_t*>(args.out);
 #pragma unroll
