@@ -120,6 +120,16 @@ fufft_status fufft_pipeline_v16_bfp(const short2* aq, const float* a_scale, cons
 }
 
 // split forward / apply, radix-8 chain (fufft.cuh:1343, :1375)
+// natural-order forward c2c, N = 8^LOG8N (Mode A, fufft.cuh:878-904)
+template<int N, int LOG8N, int CPB>
+fufft_status fufft_c2c(const float2* in, float2* out, unsigned int* timing, long long batch, cudaStream_t stream = 0)
+{
+   static_assert(N == detail::ipow(8, LOG8N), "N must equal 8^LOG8N");
+   (void)timing;
+   return fufft_c2c_f32(reinterpret_cast<const float*>(in), reinterpret_cast<float*>(out), N, batch, -1,
+                        detail::st(stream));
+}
+
 template<int N, int LEAD, int NR8, int CPB>
 fufft_status fufft_pipeline_fwd(const float2* a, float2* spec, unsigned int* timing, long long batch,
                                 cudaStream_t stream = 0)

@@ -57,6 +57,8 @@ int main(int argc, char** argv)
    if(dump(dir, "out_v16", out, bytes)) return 1;
    OK((fufft_pipeline_v16f<N, L16, NR16, CPB>(a, bp16, out, nullptr, batch)));
    if(dump(dir, "out_v16f", out, bytes)) return 1;
+   OK((fufft_c2c<N, 4, CPB>(a, out, nullptr, batch)));   // Mode A: natural-order forward DFT
+   if(dump(dir, "out_c2c", out, bytes)) return 1;
    if(cudaDeviceSynchronize() != cudaSuccess) return 1;
    printf("ok\n");
    return 0;

@@ -43,3 +43,4 @@ def test_cpp_layer_matches_oracle(tmp_path, oracle):
     assert rel_l2(out("ip_conj"), oracle.conv(a, b8, n, 8, MID_CONJ)) <= 2e-6
     want16 = oracle.conv(a, b16, n, 16)
     assert rel_l2(out("v16"), want16) <= 2e-6 and rel_l2(out("v16f"), want16) <= 2e-6
+    assert rel_l2(out("c2c"), oracle.c2c(a, n, -1, 16)) <= 2e-6
