@@ -438,7 +438,21 @@ def run_sweep(args):
             emit(f"6: natural-order c2c {name} N={n} batch={batch}", ms, batch * n, 16)
         ms = time_steps(torch, lambda: ops.filter_from_taps(a, n, ops.LAYOUT_R16_BPERM), steps, warm, None)
         emit(f"6: filter from taps N={n} batch={batch} (R16_BPERM)", ms, batch * n, 16)
-        del a, o
+        # int16-BFP pack: abs-max pass + quantise pass over fp32 (8 + 8 read, 4 write per point)
+        ms = time_steps(torch, lambda: ops.bfp_pack(a, n), steps, warm, None)
+        emit(f"6: int16-BFP pack N={n} batch={batch} (two passes)", ms, batch * n, 20)
+        del o
+        # fused two-for-one real convolution: 2 x 2^27 real points, one real filter
+        # spectrum per pair (12 B per real point: 4+4 read, 8 filter per pair slot, 4+4 write)
+        xr = a.real.contiguous()
+        yr = a.imag.contiguous()
+        taps = torch.rand(batch, n, device="cuda", generator=g) * 2 - 1
+        bspec = ops.filter_from_taps(taps.to(torch.complex64).view(-1), n, ops.LAYOUT_R16_BPERM)
+        del a, taps
+        ms = time_steps(torch, lambda: ops.conv_r2(xr, yr, bspec, n, ops.LAYOUT_R16_BPERM), steps, warm, None)
+        emit(f"6: two-for-one real conv N={n} x {2 * batch} real signals (R16_BPERM)", ms, 2 * batch * n, 12,
+             points="real points")
+        del xr, yr, bspec
     # 7: the reference's own yardstick (its published ratios are against a
     # cuFFT chain: README.md:12-13): cuFFT forward, pointwise multiply, cuFFT
     # inverse (torch.fft, three launches), against the fused kernel, same data

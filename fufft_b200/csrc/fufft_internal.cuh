@@ -74,11 +74,13 @@ fufft_status launch_chain(const ConvArgs& args, cudaStream_t st, int device)
 #define FUFFT_L2_PREFETCH 1
 #endif
    // L2 prefetch one wave ahead: +2-3% for fp32 signals at N = 1024..4096
-   // (B200, A/B), neutral for int16-BFP, so fp32 only
-   if(FUFFT_L2_PREFETCH && IN == In::C32 && aligned(args.a, 16) &&
-      (MID == Mid::NONE || aligned(args.b, 16)) && grid > resident[device & 63].load()) {
+   // over 1 GiB (B200, A/B), neutral for int16-BFP, and -7% for a launch of
+   // 3-4 waves (N=1024 x 4096), so fp32 launches of 8 waves or more only
+   const long long res = resident[device & 63].load();
+   if(FUFFT_L2_PREFETCH && IN == In::C32 && aligned(args.a, 16) && (MID == Mid::NONE || aligned(args.b, 16)) &&
+      res > 0 && grid >= 8 * res) {
       ConvArgs a2 = args;
-      a2.prefetch_ahead = resident[device & 63].load();
+      a2.prefetch_ahead = res;
       kern<<<(unsigned)grid, K::THREADS, K::SMEM, st>>>(a2);
    } else {
       kern<<<(unsigned)grid, K::THREADS, K::SMEM, st>>>(args);
