@@ -14,6 +14,7 @@ static fufft_status launch_cluster(const ConvArgs& args, cudaStream_t st, int de
    using K = ClusterConv<Inner, C, OUT_L, OUT_SHIFT, MID, FLT, BFP>;
    auto kern = conv_cluster_kernel<Inner, C, OUT_L, OUT_SHIFT, MID, FLT, BFP>;
    static std::atomic<uint64_t> configured{0}, usable{0};
+   static std::atomic<int> wave[64];   // clusters resident at once
    const uint64_t bit = 1ull << (device & 63);
    cudaLaunchConfig_t cfg = {};
    cudaLaunchAttribute attr[1];
@@ -40,11 +41,23 @@ static fufft_status launch_cluster(const ConvArgs& args, cudaStream_t st, int de
          nclusters = 0;
       }
       if(nclusters > 0) usable.fetch_or(bit);
+      wave[device & 63].store(nclusters);
       configured.fetch_or(bit, std::memory_order_acq_rel);
    }
    if(!(usable.load() & bit)) return FUFFT_ERR_UNSUPPORTED;
    cfg.gridDim = dim3((unsigned)(args.batch * C));
-   fufft_status s = check(cudaLaunchKernelEx(&cfg, kern, args));
+#ifndef FUFFT_CLUSTER_L2_PREFETCH
+#define FUFFT_CLUSTER_L2_PREFETCH 1
+#endif
+   // L2 prefetch one cluster wave ahead, for launches of eight waves or more;
+   // the bulk prefetches want 16-byte aligned rows
+   ConvArgs a2 = args;
+   const int w = wave[device & 63].load();
+   const int eb = BFP ? 4 : 8;
+   if(FUFFT_CLUSTER_L2_PREFETCH && w > 0 && args.batch >= 8LL * w && aligned(args.a, 16) &&
+      (K::B / C) * eb % 16 == 0 && (MID == Mid::NONE || (aligned(args.b, 16) && args.filter_stride % 4 == 0)))
+      a2.prefetch_ahead = w;
+   fufft_status s = check(cudaLaunchKernelEx(&cfg, kern, a2));
    if(s == FUFFT_OK) count_launch();
    return s;
 }

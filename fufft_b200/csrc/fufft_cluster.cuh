@@ -192,6 +192,22 @@ struct ClusterConv {
       __syncthreads();
       cluster_arrive_relaxed();
 
+      // ---- L2 prefetch: the column slice and filter block of the transform
+      // this CTA's slot takes one cluster wave later
+      if(lane == 0 && args.prefetch_ahead > 0 && tr + args.prefetch_ahead < args.batch) {
+         constexpr uint32_t EB = BFP ? 4 : 8;
+         const long long nt = tr + args.prefetch_ahead;
+         const unsigned char* a = static_cast<const unsigned char*>(args.a);
+#pragma unroll 1
+         for(int q = 0; q < C; ++q)
+            prefetch_l2_bulk(a + ((size_t)nt * NT + (size_t)q * B + (size_t)c * CB) * EB, (uint32_t)(CB * EB));
+         if constexpr(HAS_FILTER)
+            if(args.filter_stride != 0)
+               prefetch_l2_bulk(static_cast<const unsigned char*>(args.b) +
+                                   ((size_t)(nt * args.filter_stride) + (size_t)c * B) * FELEM,
+                                (uint32_t)(B * FELEM));
+      }
+
       // ---- this CTA's filter block (row c of the chain order), TMA bulk prefetch
       if constexpr(HAS_FILTER && FLT == Flt::SMEM) {
          if(lane == 0) {
