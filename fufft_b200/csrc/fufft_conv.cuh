@@ -38,8 +38,10 @@ namespace fufft {
 enum class In { C32, BFP, REAL2, SPEC, SPEC_BP };
 enum class Out { C32, BFP, REAL2, SPEC, SPEC_BP, NAT };
 enum class Mid { NONE, MUL, CONJ };        // pointwise operation between the transforms
-enum class Flt { NONE, SMEM, GLOBAL };     // filter read: TMA-staged register-boundary
-                                           // layout, or chain order straight from HBM
+// filter read: register-boundary layout staged by a TMA bulk copy (SMEM) or
+// read straight from global memory (BP_DIRECT: coalesced, no shared memory),
+// or chain order straight from global memory (GLOBAL)
+enum class Flt { NONE, SMEM, GLOBAL, BP_DIRECT };
 
 __host__ __device__ constexpr int ilog2c(long long n) { return n <= 1 ? 0 : 1 + ilog2c(n / 2); }
 
@@ -466,7 +468,12 @@ struct ConvKernel {
       } else {
          if constexpr(MID != Mid::NONE) {
             float2 f[R];
-            if constexpr(FLT == Flt::SMEM) {
+            if constexpr(FLT == Flt::BP_DIRECT) {
+               static_assert(!FBFP, "fp32 filters only");
+               const float2* fb = static_cast<const float2*>(args.b) + (size_t)filter_off(args, tr) + lane;
+#pragma unroll
+               for(int k = 0; k < R; ++k) f[k] = active ? __ldg(fb + k * T) : make_float2(0.f, 0.f);
+            } else if constexpr(FLT == Flt::SMEM) {
                mbar_wait(&fbar, 0, args.status);
                if constexpr(FBFP) {
                   const uint32_t* Fs = reinterpret_cast<const uint32_t*>(F) + off;
@@ -575,9 +582,15 @@ template<int THREADS, int RESIDENT = FUFFT_RESIDENT_THREADS> constexpr int min_b
 
 // natural-order output (one transform direction, no filter): three CTAs per
 // SM, as the spectrum-output kernels reach on their own (~80 registers)
+#ifndef FUFFT_RESIDENT_THREADS_APPLY
+#define FUFFT_RESIDENT_THREADS_APPLY 1024
+#endif
 template<In IN, Out OUT> constexpr int resident_threads()
 {
-   return IN == In::BFP ? FUFFT_RESIDENT_THREADS_BFP : OUT == Out::NAT ? 768 : FUFFT_RESIDENT_THREADS;
+   return IN == In::BFP ? FUFFT_RESIDENT_THREADS_BFP
+        : OUT == Out::NAT ? 768
+        : IN == In::SPEC_BP ? FUFFT_RESIDENT_THREADS_APPLY
+                            : FUFFT_RESIDENT_THREADS;
 }
 
 template<class C, int CPB, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>

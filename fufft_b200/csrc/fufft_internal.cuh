@@ -202,6 +202,11 @@ fufft_status dispatch_mid(int n, fufft_midop mid, bool bperm, const ConvArgs& a,
 // split apply: the spectrum comes in the layout family of the filter --
 // register-boundary order with the TMA-staged bperm filter, chain order with
 // the chain-order filter
+#ifndef FUFFT_APPLY_FILTER_DIRECT
+#define FUFFT_APPLY_FILTER_DIRECT 1
+#endif
+constexpr Flt APPLY_FLT = FUFFT_APPLY_FILTER_DIRECT ? Flt::BP_DIRECT : Flt::SMEM;
+
 template<int R, Out OUT>
 fufft_status dispatch_apply(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
 {
@@ -210,10 +215,10 @@ fufft_status dispatch_apply(int n, fufft_midop mid, bool bperm, const ConvArgs& 
       return bperm ? launch_n<R, In::SPEC_BP, OUT, Mid::NONE, Flt::NONE, false>(n, a, st, dev)
                    : launch_n<R, In::SPEC, OUT, Mid::NONE, Flt::NONE, false>(n, a, st, dev);
    case FUFFT_MID_MULTIPLY:
-      return bperm ? launch_n<R, In::SPEC_BP, OUT, Mid::MUL, Flt::SMEM, false>(n, a, st, dev)
+      return bperm ? launch_n<R, In::SPEC_BP, OUT, Mid::MUL, APPLY_FLT, false>(n, a, st, dev)
                    : launch_n<R, In::SPEC, OUT, Mid::MUL, Flt::GLOBAL, false>(n, a, st, dev);
    case FUFFT_MID_CONJ_MULTIPLY:
-      return bperm ? launch_n<R, In::SPEC_BP, OUT, Mid::CONJ, Flt::SMEM, false>(n, a, st, dev)
+      return bperm ? launch_n<R, In::SPEC_BP, OUT, Mid::CONJ, APPLY_FLT, false>(n, a, st, dev)
                    : launch_n<R, In::SPEC, OUT, Mid::CONJ, Flt::GLOBAL, false>(n, a, st, dev);
    }
    return FUFFT_ERR_INVALID_ARG;
