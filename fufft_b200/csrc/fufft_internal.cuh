@@ -235,28 +235,17 @@ fufft_status dispatch_apply(int n, fufft_midop mid, bool bperm, const ConvArgs& 
 template<int R, bool BFP>
 fufft_status dispatch_conv(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
 {
-   const int eb = BFP ? 4 : 8;
-#ifdef FUFFT_NO_STREAM
-   const bool ok = false;
-#else
-   const bool ok = !BFP && !bperm && mid != FUFFT_MID_NONE && n * eb >= 128 && aligned(a.a, 16) &&
-                   aligned(a.b, 16) && (a.filter_stride * eb) % 128 == 0;
-#endif
-   if(ok) {
-      fufft_status s = FUFFT_ERR_UNSUPPORTED;
-      switch(mid) {
-      case FUFFT_MID_NONE: s = launch_stream_n<R, BFP, Mid::NONE, false>(n, a, st, dev); break;
-      case FUFFT_MID_MULTIPLY:
-         s = bperm ? launch_stream_n<R, BFP, Mid::MUL, false>(n, a, st, dev)
-                   : launch_stream_n<R, BFP, Mid::MUL, true>(n, a, st, dev);
-         break;
-      case FUFFT_MID_CONJ_MULTIPLY:
-         s = bperm ? launch_stream_n<R, BFP, Mid::CONJ, false>(n, a, st, dev)
-                   : launch_stream_n<R, BFP, Mid::CONJ, true>(n, a, st, dev);
-         break;
+#ifndef FUFFT_NO_STREAM
+   // fp32 signal with a multiply / conjugate-multiply filter in the linear chain order
+   if constexpr(!BFP) {
+      if(!bperm && mid != FUFFT_MID_NONE && n * 8 >= 128 && aligned(a.a, 16) && aligned(a.b, 16) &&
+         (a.filter_stride * 8) % 128 == 0) {
+         const fufft_status s = mid == FUFFT_MID_MULTIPLY ? launch_stream_n<R, false, Mid::MUL, true>(n, a, st, dev)
+                                                          : launch_stream_n<R, false, Mid::CONJ, true>(n, a, st, dev);
+         if(s != FUFFT_ERR_UNSUPPORTED) return s;
       }
-      if(s != FUFFT_ERR_UNSUPPORTED) return s;
    }
+#endif
    return BFP ? dispatch_mid<R, In::BFP, Out::BFP, true>(n, mid, bperm, a, st, dev)
               : dispatch_mid<R, In::C32, Out::C32, false>(n, mid, bperm, a, st, dev);
 }
