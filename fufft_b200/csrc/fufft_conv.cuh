@@ -203,6 +203,33 @@ __device__ __forceinline__ void xload(const float2* X, int off, float2 (&x)[C::R
 __device__ __forceinline__ void sched_fence() { asm volatile("" ::: "memory"); }
 
 
+// The exchange between passes p and p+1 is warp-local when every position's
+// owner in pass p and its owner in pass p+1 (lane of its butterfly group,
+// visit() above) sit in the same warp.  Every thread writes exactly the
+// positions it owns in the pass it read, so between two block-wide barriers
+// each position is touched only by the threads of one warp along a run of
+// warp-local exchanges, and __syncwarp orders them.  (Radix-16 chains: the
+// last exchange of each direction moves data within 16-lane groups.)
+template<class C, int p>
+constexpr bool warp_local_exchange()
+{
+   if(C::T <= 32) return true;
+   const int r0 = C::radix(p), M0 = C::stride(p), r1 = C::radix(p + 1), M1 = C::stride(p + 1);
+   for(int P = 0; P < C::N; ++P) {
+      const int g0 = (P / (r0 * M0)) * M0 + P % M0;
+      const int g1 = (P / (r1 * M1)) * M1 + P % M1;
+      if((g0 % C::T) / 32 != (g1 % C::T) / 32) return false;
+   }
+   return true;
+}
+
+#ifndef FUFFT_WARP_LOCAL_SYNC
+#define FUFFT_WARP_LOCAL_SYNC 1
+#endif
+// barrier of the exchange between passes p and p+1
+template<class C, int p, int CPB>
+__device__ __forceinline__ void exchange_sync(int slot);
+
 // barrier over the T threads of one transform
 template<int T, int CPB>
 __device__ __forceinline__ void slot_sync(int slot)
@@ -210,6 +237,13 @@ __device__ __forceinline__ void slot_sync(int slot)
    if constexpr(T <= 32) __syncwarp();
    else if constexpr(CPB == 1) __syncthreads();
    else asm volatile("bar.sync %0, %1;" :: "r"(slot + 1), "n"(T) : "memory");
+}
+
+template<class C, int p, int CPB>
+__device__ __forceinline__ void exchange_sync(int slot)
+{
+   if constexpr(FUFFT_WARP_LOCAL_SYNC && warp_local_exchange<C, p>()) __syncwarp();
+   else slot_sync<C::T, CPB>(slot);
 }
 
 // int16 pair <-> fp32 complex, the reference's BFP element (fufft.cuh:1572-1612)
@@ -290,7 +324,7 @@ struct ConvKernel {
       sched_fence();
       if constexpr(p > 0) {
          xstore<C, p - 1>(X, off, x, lane);
-         slot_sync<T, CPB>(slot);
+         exchange_sync<C, p - 1, CPB>(slot);
          xload<C, p>(X, off, x, lane);
       }
       butterflies<C, p, -1>(x, lane, tw);
@@ -303,7 +337,7 @@ struct ConvKernel {
       sched_fence();
       if constexpr(p < C::NP - 1) {
          xstore<C, p + 1>(X, off, x, lane);
-         slot_sync<T, CPB>(slot);
+         exchange_sync<C, p, CPB>(slot);
          xload<C, p>(X, off, x, lane);
       }
       butterflies<C, p, +1>(x, lane, tw);

@@ -157,3 +157,33 @@ def test_natural_order_scatter(n):
         rd.append([swz(slot * n + lane + T * u) for u in range(R)])
     assert worst_ways(scat, 8) <= 2
     assert worst_ways(rd, 8) == 1
+
+
+def warp_local(n, R, p):
+    """fufft_conv.cuh warp_local_exchange<C, p>(): every position's owner in
+    pass p and in pass p+1 share a warp"""
+    T = n // R
+    if T <= 32:
+        return True
+    (r0, M0), (r1, M1) = passes(n, R)[p], passes(n, R)[p + 1]
+    for P in range(n):
+        g0 = (P // (r0 * M0)) * M0 + P % M0
+        g1 = (P // (r1 * M1)) * M1 + P % M1
+        if (g0 % T) // 32 != (g1 % T) // 32:
+            return False
+    return True
+
+
+@pytest.mark.parametrize("n", [1024, 2048, 4096, 8192])
+def test_last_exchange_is_warp_local(n):
+    """radix-16 chains: the exchange into the M=1 pass stays inside 16-lane
+    groups (warp barrier), the first one spans the block (block barrier); the
+    owner maps are partitions of the n positions"""
+    R = 16
+    k = len(passes(n, R))
+    assert warp_local(n, R, k - 2)
+    assert not warp_local(n, R, 0)
+    for p in range(k):
+        r, M = passes(n, R)[p]
+        owners = [(P // (r * M)) * M + P % M for P in range(n)]
+        assert sorted(owners) == sorted(list(range(n // r)) * r)
