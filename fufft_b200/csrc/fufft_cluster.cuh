@@ -111,7 +111,7 @@ struct ClusterConv {
       sched_fence();
       if constexpr(p > 0) {
          xstore<I, p - 1>(X, 0, x, lane);
-         __syncthreads();
+         exchange_sync<I, p - 1, 1>(0);
          xload<I, p>(X, 0, x, lane);
       }
       butterflies<I, p, -1>(x, lane, tw);
@@ -122,7 +122,7 @@ struct ClusterConv {
       sched_fence();
       if constexpr(p < I::NP - 1) {
          xstore<I, p + 1>(X, 0, x, lane);
-         __syncthreads();
+         exchange_sync<I, p, 1>(0);
          xload<I, p>(X, 0, x, lane);
       }
       butterflies<I, p, +1>(x, lane, tw);
