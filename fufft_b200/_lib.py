@@ -29,6 +29,7 @@ SIGNATURES = {
     "fufft_init": (_I, []),
     "fufft_device_status": (_I, [ct.POINTER(_U32), _P]),
     "fufft_launch_count": (ct.c_uint64, []),
+    "fufft_selftest_wait_timeout": (_I, [_U32, _P]),
     "fufft_chain": (_I, [_I, _I, ct.POINTER(_I)]),
     "fufft_chain_rev": (_I64, [_I64, ct.POINTER(_I), _I]),
     "fufft_filter_permute_host": (_I, [_P, _P, _I, _I, _I]),

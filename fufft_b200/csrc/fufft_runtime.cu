@@ -31,6 +31,19 @@ __global__ void twiddle_init_kernel()
    }
 }
 
+// self-test of the bounded waits: an mbarrier that nothing will complete,
+// waited on with a short limit by one thread, which must give up, record
+// STATUS_TMA_TIMEOUT and return like every waiting kernel of the library
+__global__ void wait_timeout_selftest_kernel(unsigned int* status, uint32_t limit_us)
+{
+   __shared__ uint64_t bar;
+   if(threadIdx.x == 0) {
+      mbar_init(&bar, 1);
+      fence_mbar_init();
+      mbar_wait(&bar, 0, status, (uint64_t)limit_us * 1000ull);
+   }
+}
+
 namespace host {
 
 namespace {
@@ -353,6 +366,16 @@ fufft_status fufft_device_status(uint32_t* status_out, fufft_stream_t stream)
 }
 
 uint64_t fufft_launch_count(void) { return host::g_launches.load(); }
+
+fufft_status fufft_selftest_wait_timeout(uint32_t limit_us, fufft_stream_t stream)
+{
+   if(limit_us == 0 || limit_us > 1000000) return FUFFT_ERR_INVALID_ARG;
+   host::DeviceCtx c;
+   fufft_status s = host::device_ctx(&c);
+   if(s != FUFFT_OK) return s;
+   wait_timeout_selftest_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(c.status, limit_us);
+   return host::check(cudaGetLastError());
+}
 
 int fufft_chain(int n, int radix, int* radices_out)
 {

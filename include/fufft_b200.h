@@ -96,6 +96,12 @@ fufft_status fufft_init(void);
 fufft_status fufft_device_status(uint32_t* status_out, fufft_stream_t stream);
 /* number of fused-kernel launches this process has issued (all threads) */
 uint64_t fufft_launch_count(void);
+/* self-test of the bounded device waits: one thread waits limit_us
+ * microseconds (1 .. 1e6) on an mbarrier that nothing completes, gives up and
+ * sets bit 0 of the device status word, as any library kernel whose TMA copy
+ * or peer data never arrived would; the context stays usable.  No reference
+ * counterpart (the reference's kernels have no bounded waits). */
+fufft_status fufft_selftest_wait_timeout(uint32_t limit_us, fufft_stream_t stream);
 
 /* ---- index maps (host) -------------------------------------------------- */
 /* radix chain of a one-kernel transform: [lead, R, ..., R]; returns its
