@@ -508,11 +508,13 @@ def run_sweep(args):
 def run_reference(args, rank, world):
     if rank != 0:
         return None
-    # each step: a bounded sample of the workload on every host core
+    # each step: a bounded sample of the workload on every host core, sized so
+    # the whole run stays near 90 s whatever --steps / --warmup ask for
     rates = []
     kind = cores = sample = None
+    per_step = min(args.ref_seconds, 90.0 / max(1, args.warmup + args.steps))
     for i in range(args.warmup + args.steps):
-        rate, kind, cores, sample = cpu_reference_rate(args.ref_seconds)
+        rate, kind, cores, sample = cpu_reference_rate(per_step)
         if i >= args.warmup:
             rates.append(rate)
     v = statistics.median(rates) / 1e9
