@@ -314,7 +314,7 @@ def run_dist(args, rank, world, dist):
     """one 2^26-point signal over `world` GPUs (config 5), two all-to-alls"""
     import torch
     from fufft_b200 import ops
-    from fufft_b200.distributed import GpuBackend, conv_distributed
+    from fufft_b200.distributed import GpuBackend, PeerBlocks, conv_distributed, conv_distributed_p2p
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     ops.init()
@@ -326,14 +326,23 @@ def run_dist(args, rank, world, dist):
     x0 = torch.randn(world * plan.cols, dtype=torch.complex64, device=dev, generator=g)
     bb = torch.randn(plan.n_blk, dtype=torch.complex64, device=dev, generator=g) / n
     x = x0.clone()
-    ms = time_steps(torch, lambda: conv_distributed(x, bb, n, backend=be, plan=plan), args.steps, args.warmup, dist)
+    if args.dist_mode == "p2p":
+        peers = PeerBlocks(plan.n_blk)
+        ms = time_steps(torch, lambda: conv_distributed_p2p(x, bb, n, peers, backend=be, plan=plan), args.steps,
+                        args.warmup, dist)
+        peers.close()
+    else:
+        ms = time_steps(torch, lambda: conv_distributed(x, bb, n, backend=be, plan=plan), args.steps, args.warmup,
+                        dist)
     hbm, _ = peaks()
     return {"metric": "distributed single-signal fused conv Gpoints/s, N=2^26", "value": round(n / (ms * 1e-3) / 1e9, 3),
             "unit": "Gpoints/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic", "config": {"workload": "configs[4] single N=2^26 signal",
             "plan": {"block": plan.n_blk, "r_out": plan.r_out, "mid": plan.mid, "chain": plan.chain},
-            "nvlink_bytes_per_gpu": 2 * 8 * plan.n_blk * (world - 1) // world}}
+            "nvlink_bytes_per_gpu": 2 * 8 * plan.n_blk * (world - 1) // world,
+            "exchange": "NVLink stores / loads fused into the outer passes" if args.dist_mode == "p2p"
+                        else "NCCL all_to_all"}}
 
 
 def time_flushed(torch, fn, steps, warmup, flush_bytes=512 << 20):
@@ -542,6 +551,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-case", nargs="?", const="headline", default=None, choices=["headline", "cluster"],
                     help="one launch per kernel of a group, for ncu")
+    ap.add_argument("--dist-mode", choices=["p2p", "nccl"], default="p2p",
+                    help="dist: all-to-alls fused into the outer passes over NVLink (p2p) or NCCL all_to_all")
     ap.add_argument("--configs", default="1,2,3,4,5,6,7",
                     help="sweep: which BASELINE.json configs (1-based); 6 = c2c and filter preparation, "
                          "7 = the cuFFT chain the reference compares against")

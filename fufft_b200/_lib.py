@@ -56,6 +56,12 @@ SIGNATURES = {
     "fufft_conv_large_bfp": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _I, _P, ct.c_size_t, _P]),
     "fufft_conv_large_bfp_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _I, _P]),
     "fufft_dist_pass": (_I, [_P, _I, _I64, _I64, _I64, _I, _P]),
+    "fufft_dist_pass_push": (_I, [_P, _P, _I, _I, _I64, _I64, _P]),
+    "fufft_dist_pass_pull": (_I, [_P, _P, _I, _I, _I64, _I64, _P]),
+    "fufft_peer_alloc": (_I, [ct.c_size_t, ct.POINTER(_P), _P]),
+    "fufft_peer_open": (_I, [_P, ct.POINTER(_P)]),
+    "fufft_peer_close": (_I, [_P]),
+    "fufft_peer_free": (_I, [_P]),
 }
 
 

@@ -24,9 +24,18 @@ chain-ordered filter, so each rank needs only its n/W filter slice.
 
 Compute goes through a backend object (GPU: this library; the CPU tests plug
 in the oracle), so the partition and exchange logic is tested under gloo.
+
+conv_distributed_p2p is the same scheme with the all-to-alls fused into the
+outer passes over NVLink peer memory: every rank's n/W block buffer is mapped
+into all ranks (CUDA IPC, PeerBlocks); step 1+2 become one kernel that stores
+row k's results straight into rank k's block (fufft_dist_pass_push), step 4+5
+one kernel that loads them back from the blocks (fufft_dist_pass_pull).  The
+ranks only synchronise (a one-element all-reduce on the stream) between the
+phases; no signal data goes through NCCL.
 """
 from __future__ import annotations
 
+import ctypes as ct
 from dataclasses import dataclass
 
 import torch
@@ -84,6 +93,83 @@ class GpuBackend:
         else:
             self.ops.conv_large(block, b_block, plan.n_blk, self.ops.LAYOUT_R16, r_out=plan.r_out,
                                 mid_size=plan.mid)
+
+
+class _DeviceArray:
+    """a device float32 array at a raw address, for torch.as_tensor"""
+
+    def __init__(self, ptr: int, count: int):
+        self.__cuda_array_interface__ = {"shape": (count,), "typestr": "<f4", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerBlocks:
+    """This rank's block buffer (n_blk complex points) and the mapping of every
+    rank's one into this process; `block` is this rank's buffer as a complex64
+    tensor, `addresses` the host array of the world block addresses."""
+
+    def __init__(self, n_blk: int, group=None):
+        from ._lib import check, lib
+        self.L, self.check = lib(), check
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        own, handle = ct.c_void_p(), (ct.c_char * 64)()
+        check(self.L.fufft_peer_alloc(n_blk * 8, ct.byref(own), handle), "fufft_peer_alloc")
+        self.own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.mapped, ptrs = [], []
+        for k, h in enumerate(handles):
+            if k == self.rank:
+                ptrs.append(self.own)
+                continue
+            p = ct.c_void_p()
+            check(self.L.fufft_peer_open(h, ct.byref(p)), "fufft_peer_open")
+            self.mapped.append(p.value)
+            ptrs.append(p.value)
+        self.addresses = (ct.c_uint64 * self.world)(*ptrs)
+        flat = torch.as_tensor(_DeviceArray(self.own, 2 * n_blk), device="cuda")
+        self.block = torch.view_as_complex(flat.view(-1, 2))
+
+    def close(self, group=None):
+        """unmap the peers' buffers; once every rank has, free this rank's own
+        (a collective call: every rank of the group makes it)"""
+        torch.cuda.current_stream().synchronize()
+        for p in self.mapped:
+            self.check(self.L.fufft_peer_close(p), "fufft_peer_close")
+        self.mapped = []
+        dist.barrier(group=group)
+        if self.own:
+            self.block = None
+            self.check(self.L.fufft_peer_free(self.own), "fufft_peer_free")
+            self.own = 0
+
+
+def _stream_barrier(group, flag: torch.Tensor) -> None:
+    """every rank's earlier work on the current stream is done before its later work starts"""
+    dist.all_reduce(flag, group=group)
+
+
+def conv_distributed_p2p(x_local: torch.Tensor, b_block: torch.Tensor, n: int, peers: PeerBlocks,
+                         backend=None, group=None, plan: DistPlan | None = None) -> torch.Tensor:
+    """conv_distributed with the all-to-alls fused into the outer passes as
+    NVLink stores / loads; same arguments plus the mapped block buffers"""
+    backend = backend or GpuBackend()
+    world, rank = peers.world, peers.rank
+    plan = plan or backend.plan(n, world)
+    if x_local.numel() != world * plan.cols or b_block.numel() != plan.n_blk or peers.block.numel() != plan.n_blk:
+        raise ValueError("slice sizes do not match the plan")
+    flag = torch.zeros(1, device=x_local.device)
+    st = torch.cuda.current_stream().cuda_stream
+    xp = torch.view_as_real(x_local).data_ptr() if x_local.is_complex() else x_local.data_ptr()
+    backend.check(backend.lib().fufft_dist_pass_push(xp, peers.addresses, world, rank, plan.cols, n, st),
+                  "fufft_dist_pass_push")
+    _stream_barrier(group, flag)
+    backend.conv_block(peers.block, b_block, plan)
+    _stream_barrier(group, flag)
+    backend.check(backend.lib().fufft_dist_pass_pull(xp, peers.addresses, world, rank, plan.cols, n, st),
+                  "fufft_dist_pass_pull")
+    _stream_barrier(group, flag)   # the peers are done reading this rank's block
+    return x_local
 
 
 def scatter_signal(x: torch.Tensor, n: int, world: int, rank: int) -> torch.Tensor:

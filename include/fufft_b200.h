@@ -290,6 +290,30 @@ fufft_status fufft_conv_large_bfp(const int16_t* aq, const float* a_scale, const
 fufft_status fufft_dist_pass(float* x_local, int world, int64_t cols, int64_t col0, int64_t n, int sign,
                              fufft_stream_t stream);
 
+/* The same passes with the all-to-all fused in, over NVLink peer memory:
+ * every rank holds an n/world-point block buffer mapped into all ranks
+ * (fufft_peer_alloc / fufft_peer_open); peer_blocks is a HOST array of the
+ * world block addresses as seen from this process (this rank's own at index
+ * rank).  push: the first DIF pass of this rank's columns, row k's results
+ * stored straight into rank k's block at offset rank*cols.  pull: the last
+ * DIT pass, row k's inputs loaded straight from rank k's block.  Between push
+ * and the block convolution, and between it and pull, every rank must have
+ * finished (a barrier on the stream, e.g. a one-element all-reduce). */
+fufft_status fufft_dist_pass_push(const float* x_local, const uint64_t* peer_blocks, int world, int rank,
+                                  int64_t cols, int64_t n, fufft_stream_t stream);
+fufft_status fufft_dist_pass_pull(float* x_local, const uint64_t* peer_blocks, int world, int rank, int64_t cols,
+                                  int64_t n, fufft_stream_t stream);
+
+/* Device buffers the other processes of the node can map (CUDA IPC).
+ * alloc: `bytes` of device memory and its FUFFT_IPC_HANDLE_BYTES-byte handle;
+ * open: map a handle from another process (FUFFT_ERR_PEER_UNAVAILABLE if the
+ * GPUs cannot reach each other); close: unmap; free: release own buffer. */
+#define FUFFT_IPC_HANDLE_BYTES 64
+fufft_status fufft_peer_alloc(size_t bytes, void** dev_ptr, void* ipc_handle);
+fufft_status fufft_peer_open(const void* ipc_handle, void** dev_ptr);
+fufft_status fufft_peer_close(void* dev_ptr);
+fufft_status fufft_peer_free(void* dev_ptr);
+
 /* The same BFP four-step for callers that cannot allocate device memory when
  * they call the library (a host whose device memory is entirely held by its
  * own pool allocator, or a latency-critical loop where an allocation's

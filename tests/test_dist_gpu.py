@@ -1,6 +1,8 @@
-"""The distributed single-signal convolution on 2, 4 and 8 GPUs (NCCL),
-against the host simulation of the same scheme (oracle.conv_dist) and fp64.
-Each world size is skipped when fewer GPUs are visible."""
+"""The distributed single-signal convolution on 2, 4 and 8 GPUs, with the
+all-to-alls through NCCL and fused into the outer passes as NVLink stores /
+loads (p2p), against the host simulation of the same scheme
+(oracle.conv_dist) and fp64.  Each world size is skipped when fewer GPUs are
+visible."""
 import os
 import socket
 import subprocess
@@ -24,16 +26,17 @@ def _port():
     return p
 
 
+@pytest.mark.parametrize("mode", ["nccl", "p2p"])
 @pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("n", [1 << 16, 1 << 20])
-def test_distributed_conv(oracle, tmp_path, n, world):
+def test_distributed_conv(oracle, tmp_path, n, world, mode):
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     out = str(tmp_path / "y.npy")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
-           os.path.join(HERE, "dist_gpu_worker.py"), str(n), out]
+           os.path.join(HERE, "dist_gpu_worker.py"), str(n), out, mode]
     r = subprocess.run(cmd, capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stderr[-3000:]
     got = np.load(out)
