@@ -269,6 +269,103 @@ def run_ours(args, rank, world, dist):
     return line
 
 
+def run_ncu_all():
+    """one launch of every kernel family of the library (sizes > L2 where the
+    kernel streams HBM), for a one-table ncu summary.  Prints a manifest:
+    one line per library call, in launch order, with the points it covers and
+    its algorithmic HBM bytes."""
+    import torch
+    from fufft_b200 import ops
+    from fufft_b200._lib import check, lib
+    ops.init()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7)
+    C = torch.complex64
+    n, batch = 4096, 16384                       # 0.5 GiB of fp32 signal
+    pts = n * batch
+    a = torch.randn(pts, dtype=C, device="cuda", generator=g)
+    b = torch.randn(pts, dtype=C, device="cuda", generator=g) / n
+    o = torch.empty_like(a)
+    man = []
+
+    def call(label, fn, points, nbytes, launches=1):
+        fn()
+        torch.cuda.synchronize()
+        man.append((label, launches, points, nbytes))
+
+    call("conv fp32 R16_BPERM (register-boundary filter, TMA)", lambda: ops.conv(a, b, n, ops.LAYOUT_R16_BPERM, out=o), pts, 24 * pts)
+    call("conv fp32 R16 (linear filter: pipelined kernel)", lambda: ops.conv(a, b, n, ops.LAYOUT_R16, out=o), pts, 24 * pts)
+    call("conv fp32 R8_BPERM", lambda: ops.conv(a, b, n, ops.LAYOUT_R8_BPERM, out=o), pts, 24 * pts)
+    call("conv fp32 R16_BPERM conj-multiply", lambda: ops.conv(a, b, n, ops.LAYOUT_R16_BPERM, ops.MID_CONJ_MULTIPLY, out=o), pts, 24 * pts)
+    aq, as_ = ops.bfp_pack(a, n)
+    torch.cuda.synchronize()
+    man.append(("bfp_pack: abs-max, quantise, scale kernels", 3, pts, 20 * pts))
+    bq, bs = ops.bfp_pack(b, n)
+    torch.cuda.synchronize()
+    man.append(("bfp_pack (filter)", 3, pts, 20 * pts))
+    call("conv int16-BFP R16", lambda: ops.conv_bfp(aq, as_, bq, bs, n, ops.LAYOUT_R16), pts, 12 * pts + 12 * batch)
+    call("conv int16-BFP R16_BPERM", lambda: ops.conv_bfp(aq, as_, bq, bs, n, ops.LAYOUT_R16_BPERM), pts, 12 * pts + 12 * batch)
+    call("bfp_unpack", lambda: ops.bfp_unpack(aq, as_, n), pts, 12 * pts)
+    del aq, bq
+    call("fwd (split forward, R16_BPERM spectrum)", lambda: ops.fwd(a, n, ops.LAYOUT_R16_BPERM), pts, 16 * pts)
+    spec = ops.fwd(a, n, ops.LAYOUT_R16_BPERM)
+    torch.cuda.synchronize()
+    man.append(("fwd (spectrum for apply)", 1, pts, 16 * pts))
+    call("apply (split apply, R16_BPERM)", lambda: ops.apply(spec, b, n, ops.LAYOUT_R16_BPERM, out=o), pts, 24 * pts)
+    xr, yr = a.real.contiguous(), a.imag.contiguous()
+    torch.cuda.synchronize()
+    man.append(("(torch copies of re / im)", 2, 0, 0))
+    call("conv_r2 two-for-one real", lambda: ops.conv_r2(xr, yr, b, n, ops.LAYOUT_R16_BPERM), 2 * pts, 12 * 2 * pts)
+    call("fwd_r2 (packed real pairs)", lambda: ops.fwd_r2(xr, yr, n, ops.LAYOUT_R16_BPERM), 2 * pts, 16 * pts)
+    sp512 = spec[: 512 * n]
+    fl = b[: 256 * n]
+    og = torch.empty(2 * 512 * 256 * n, device="cuda")
+    call("apply_grid_r2 (512 pairs x 256 filters)", lambda: ops.apply_grid_r2(sp512, fl, n, ops.LAYOUT_R16_BPERM, out=og),
+         2 * 512 * 256 * n, 4 * 2 * 512 * 256 * n + 8 * n * (512 + 256))
+    del og
+    call("c2c forward (natural order)", lambda: ops.c2c(a, n, -1, out=o), pts, 16 * pts)
+    call("filter_from_taps R16_BPERM", lambda: ops.filter_from_taps(a, n, ops.LAYOUT_R16_BPERM), pts, 16 * pts)
+    call("filter_permute (device)", lambda: ops.filter_permute(a, n, ops.LAYOUT_R16_BPERM), pts, 16 * pts)
+    h = w = 64
+    call("conv2d 64x64 one CTA (shared filter)", lambda: ops.conv2d(a, b[: h * w], h, w, ops.LAYOUT_R16_BPERM, filter_stride=0, out=o),
+         pts, 16 * pts)
+    call("conv2d 256x256 cluster (shared filter)", lambda: ops.conv2d(a, b[: 65536], 256, 256, ops.LAYOUT_R16_BPERM, filter_stride=0, out=o),
+         pts, 16 * pts)
+    n2 = 32768
+    call("conv N=32768 cluster C=8", lambda: ops.conv(a, b, n2, ops.LAYOUT_R16_BPERM, out=o), pts, 24 * pts)
+    buf = a.clone()
+    torch.cuda.synchronize()
+    man.append(("(torch clone)", 1, 0, 0))
+    call("four-step N=32768 cluster C=16", lambda: ops.conv_large(buf, b, n2, ops.LAYOUT_R16_BPERM, r_out=16, mid_size=2048), pts, 24 * pts)
+    aq, as_ = ops.bfp_pack(a, n2)
+    bq, bs = ops.bfp_pack(b, n2)
+    torch.cuda.synchronize()
+    man.append(("bfp_pack x2 (four-step inputs)", 6, 0, 0))
+    call("int16-BFP four-step N=32768 cluster C=16",
+         lambda: ops.conv_large_bfp(aq, as_, bq, bs, n2, ops.LAYOUT_R16_BPERM, r_out=16, mid_size=2048),
+         pts, 12 * pts + 12 * (pts // n2))
+    del aq, bq
+    n3 = 1 << 20
+    r_out, mid = ops.large_plan(n3, ops.LAYOUT_R16)
+    lout, q = 0, n3 // mid           # outer levels: n3 = r_out^lout * mid
+    while q > 1:
+        q //= r_out
+        lout += 1
+    call(f"four-step N=2^20 multi-kernel ({lout} outer r{r_out} passes each way + middle {mid})",
+         lambda: ops.conv_large(buf, b, n3, ops.LAYOUT_R16, r_out=r_out, mid_size=mid), pts, 24 * pts,
+         launches=2 * lout + 1)
+    x = a[: 8 * (n3 // 64)].contiguous()
+    torch.cuda.synchronize()
+    man.append(("(torch copy)", 1, 0, 0))
+    call("dist_pass (radix-8 outer pass of one rank, N=2^20)",
+         lambda: check(lib().fufft_dist_pass(torch.view_as_real(x).data_ptr(), 8, n3 // 64, 0, n3, -1,
+                                             torch.cuda.current_stream().cuda_stream), "fufft_dist_pass"),
+         x.numel(), 16 * x.numel())
+    assert ops.device_status() == 0
+    for label, launches, points, nbytes in man:
+        print(json.dumps({"call": label, "launches": launches, "points": points, "algorithmic_bytes": nbytes}))
+
+
 def run_ncu_case(which: str = "headline"):
     """one launch of each kernel of a group, on a batch of a few hundred MB
     (> L2), for ncu.  headline: fp32 (register-boundary filter), fp32 (linear
@@ -549,7 +646,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=2.0, help="per-thread CPU baseline sample")
     ap.add_argument("--ref-seconds", type=float, default=1.0, help="per-thread sample per reference step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--ncu-case", nargs="?", const="headline", default=None, choices=["headline", "cluster"],
+    ap.add_argument("--ncu-case", nargs="?", const="headline", default=None, choices=["headline", "cluster", "all"],
                     help="one launch per kernel of a group, for ncu")
     ap.add_argument("--dist-mode", choices=["p2p", "nccl"], default="p2p",
                     help="dist: all-to-alls fused into the outer passes over NVLink (p2p) or NCCL all_to_all")
@@ -560,6 +657,9 @@ def main():
                     help="dist: one 2^26-point signal over all ranks (2, 4 or 8); sweep: every "
                          "BASELINE.json config on one GPU, one JSON line each")
     args = ap.parse_args()
+    if args.ncu_case == "all":
+        run_ncu_all()
+        return
     if args.ncu_case:
         run_ncu_case(args.ncu_case)
         return
