@@ -282,6 +282,23 @@ __device__ __forceinline__ int chain_natural(int p)
    }
    return out;
 }
+// the same for p = R*lane + k when the last pass has radix R: k is the last
+// digit, so chain_natural(R*lane + k) = k*T + lane_natural(lane), with the
+// lane's digits (passes 0 .. NP-2) reversed into the low bits
+template<class C>
+__device__ __forceinline__ int lane_natural(int lane)
+{
+   static_assert(C::radix(C::NP - 1) == C::R, "last pass of radix R");
+   int out = 0, pos = ilog2c(C::T), op = 0;
+#pragma unroll
+   for(int k = 0; k < C::NP - 1; ++k) {
+      const int w = ilog2c(C::radix(k));
+      pos -= w;
+      out |= ((lane >> pos) & ((1 << w) - 1)) << op;
+      op += w;
+   }
+   return out;
+}
 
 template<class C_, int CPB, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>
 struct ConvKernel {
@@ -470,7 +487,11 @@ struct ConvKernel {
          sched_fence();
          slot_sync<T, CPB>(slot);   // every thread is past its last read of X
 #pragma unroll
-         for(int k = 0; k < R; ++k) X[SwzEngine::map(off + chain_natural<C>(R * lane + k))] = x[k];
+         {
+            const int nl = off + lane_natural<C>(lane);
+#pragma unroll
+            for(int k = 0; k < R; ++k) X[SwzEngine::map(nl + k * T)] = x[k];
+         }
          slot_sync<T, CPB>(slot);
          if(active) {
             const float sgn = args.conj_io ? -1.0f : 1.0f;
