@@ -163,20 +163,66 @@ __device__ __forceinline__ void butterflies(float2 (&x)[C::R], int lane, const f
 //              of the byte address XOR bits 7..9), so a buffer filled by a
 //              swizzled TMA tensor load is already in exchange order; 1-way
 //              for every pattern with n >= 256 (radix 16) / n >= 8 (radix 8).
-struct SwzEngine { __device__ __forceinline__ static int map(int p) { return swz(p); } };
-struct Swz128 { __device__ __forceinline__ static int map(int p) { return p ^ (((p >> 4) & 7) << 1); } };
+// map(p) = p ^ term(p >> 4): the XOR term reads the bits 4 .. log2(PERIOD)-1
+// of p and writes bits 1..3, so adding a multiple of PERIOD commutes with map.
+struct SwzEngine {
+   static constexpr int PERIOD = 256;
+   __host__ __device__ static constexpr int term(int v) { return ((v ^ (v >> 1)) & 7) << 1; }
+   __device__ __forceinline__ static int map(int p) { return swz(p); }
+};
+struct Swz128 {
+   static constexpr int PERIOD = 128;
+   __host__ __device__ static constexpr int term(int v) { return (v & 7) << 1; }
+   __device__ __forceinline__ static int map(int p) { return p ^ (((p >> 4) & 7) << 1); }
+};
+
+#ifndef FUFFT_XADDR
+#define FUFFT_XADDR 1
+#endif
+// swizzled slot of every position a thread touches in pass p: f(i, slot) for
+// register i.  The swizzle is taken out of the per-element work where the
+// pass structure allows: stride M a multiple of the period -> one map per
+// group and constant offsets; stride 16 with the group base's bits 4..7 zero
+// (radix-16 pass, whole 256-point blocks) -> one XOR with a per-k constant.
+template<class C, int p, class SW, class F>
+__device__ __forceinline__ void visit_slots(int off, int lane, F&& f)
+{
+   constexpr int r = C::radix(p), M = C::stride(p), G = C::R / r, T = C::T;
+#pragma unroll
+   for(int s = 0; s < G; ++s) {
+      const int g = lane + s * T;
+      const int j = g & (M - 1);
+      const int b = g >> ilog2c(M);
+      const int P = off + b * r * M + j;
+      if constexpr(FUFFT_XADDR && M % SW::PERIOD == 0) {
+         const int q = SW::map(P);
+#pragma unroll
+         for(int k = 0; k < r; ++k) f(s * r + k, q + k * M);
+      } else if constexpr(FUFFT_XADDR && M == 16 && (r * M) % SW::PERIOD == 0 && C::N % SW::PERIOD == 0) {
+#pragma unroll
+         for(int k = 0; k < r; ++k) f(s * r + k, (P ^ SW::term(k)) + k * M);
+      } else {
+#pragma unroll
+         for(int k = 0; k < r; ++k) f(s * r + k, SW::map(P + k * M));
+      }
+   }
+}
 
 // exchange through the swizzled shared buffer; `off` = slot * N
 template<class C, int p, class SW = SwzEngine>
 __device__ __forceinline__ void xstore(float2* X, int off, const float2 (&x)[C::R], int lane)
 {
    if constexpr(C::stride(p) == 1) {
+      // base's low log2(R) bits are zero: map(base + k) = (base ^ term(base >> 4)) ^ k
       const int base = off + lane * C::R;
+      const int x0 = FUFFT_XADDR ? base ^ SW::term(base >> 4) : 0;
 #pragma unroll
-      for(int k = 0; k < C::R; k += 2)
-         *reinterpret_cast<float4*>(X + SW::map(base + k)) = make_float4(x[k].x, x[k].y, x[k + 1].x, x[k + 1].y);
+      for(int k = 0; k < C::R; k += 2) {
+         const int q = FUFFT_XADDR ? (x0 ^ k) : SW::map(base + k);
+         *reinterpret_cast<float4*>(X + q) = make_float4(x[k].x, x[k].y, x[k + 1].x, x[k + 1].y);
+      }
    } else {
-      visit<C, p>(lane, [&](int i, int pos) { X[SW::map(off + pos)] = x[i]; });
+      visit_slots<C, p, SW>(off, lane, [&](int i, int q) { X[q] = x[i]; });
    }
 }
 
@@ -185,14 +231,16 @@ __device__ __forceinline__ void xload(const float2* X, int off, float2 (&x)[C::R
 {
    if constexpr(C::stride(p) == 1) {
       const int base = off + lane * C::R;
+      const int x0 = FUFFT_XADDR ? base ^ SW::term(base >> 4) : 0;
 #pragma unroll
       for(int k = 0; k < C::R; k += 2) {
-         const float4 v = *reinterpret_cast<const float4*>(X + SW::map(base + k));
+         const int q = FUFFT_XADDR ? (x0 ^ k) : SW::map(base + k);
+         const float4 v = *reinterpret_cast<const float4*>(X + q);
          x[k] = make_float2(v.x, v.y);
          x[k + 1] = make_float2(v.z, v.w);
       }
    } else {
-      visit<C, p>(lane, [&](int i, int pos) { x[i] = X[SW::map(off + pos)]; });
+      visit_slots<C, p, SW>(off, lane, [&](int i, int q) { x[i] = X[q]; });
    }
 }
 

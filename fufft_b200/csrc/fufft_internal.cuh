@@ -61,6 +61,20 @@ fufft_status launch_chain(const ConvArgs& args, cudaStream_t st, int device)
    if(!(configured.load(std::memory_order_acquire) & bit)) {
       fufft_status s = check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)K::SMEM));
       if(s != FUFFT_OK) return s;
+#ifndef FUFFT_CARVEOUT_CAP
+#define FUFFT_CARVEOUT_CAP 1
+#endif
+      if(FUFFT_CARVEOUT_CAP) {
+         // hold the kernel at its occupancy target (resident_threads) even when
+         // it needs fewer registers than the target allows: a shared-memory
+         // carve-out that fits exactly that many CTAs (1 KB reserved per CTA),
+         // the rest of the SM's 256 KB stays L1
+         constexpr int ctas = resident_threads<IN, OUT>() >= K::THREADS ? resident_threads<IN, OUT>() / K::THREADS : 1;
+         constexpr long long need = (long long)ctas * ((long long)K::SMEM + 1024);
+         const int pct = need >= 228 * 1024 ? 100 : (int)((need * 100 + 228 * 1024 - 1) / (228 * 1024));
+         if(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, pct) != cudaSuccess)
+            cudaGetLastError();
+      }
       int nb = 0;
       if(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, K::THREADS, K::SMEM) != cudaSuccess) {
          cudaGetLastError();
