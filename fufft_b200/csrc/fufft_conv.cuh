@@ -537,8 +537,14 @@ struct ConvKernel {
 #pragma unroll
          {
             const int nl = off + lane_natural<C>(lane);
+            if constexpr(T % SwzEngine::PERIOD == 0) {
+               const int q = SwzEngine::map(nl);   // k*T leaves the swizzle's bits alone
 #pragma unroll
-            for(int k = 0; k < R; ++k) X[SwzEngine::map(nl + k * T)] = x[k];
+               for(int k = 0; k < R; ++k) X[q + k * T] = x[k];
+            } else {
+#pragma unroll
+               for(int k = 0; k < R; ++k) X[SwzEngine::map(nl + k * T)] = x[k];
+            }
          }
          slot_sync<T, CPB>(slot);
          if(active) {
