@@ -295,9 +295,21 @@ __device__ __forceinline__ void exchange_sync(int slot)
 }
 
 // int16 pair <-> fp32 complex, the reference's BFP element (fufft.cuh:1572-1612)
+#ifndef FUFFT_DEQUANT_PTX
+#define FUFFT_DEQUANT_PTX 1
+#endif
 __device__ __forceinline__ float2 bfp_dequant(uint32_t w, float scale)
 {
+#if FUFFT_DEQUANT_PTX
+   // the two int16 halves converted straight from the packed word
+   float x, y;
+   asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+       "cvt.rn.f32.s16 %0, lo;\n\tcvt.rn.f32.s16 %1, hi;\n\t}"
+       : "=f"(x), "=f"(y) : "r"(w));
+   return make_float2(x * scale, y * scale);
+#else
    return make_float2((float)(short)(w & 0xffffu) * scale, (float)(short)(w >> 16) * scale);
+#endif
 }
 // rint(clamp(v * inv, +-32767)) per component.  The float -> s16 conversion
 // saturates by definition, and |v * inv| <= 32767 * (1 + 2^-23) because inv
