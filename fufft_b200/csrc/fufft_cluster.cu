@@ -62,16 +62,24 @@ static fufft_status launch_cluster(const ConvArgs& args, cudaStream_t st, int de
    return s;
 }
 
+// register-boundary-ordered filters are read coalesced from global memory at
+// the boundary (Flt::BP_DIRECT) rather than copied to shared memory first: the
+// copy's B * 8 bytes would leave room for only two CTAs of B = 4096 per SM
+#ifndef FUFFT_CLUSTER_BP_DIRECT
+#define FUFFT_CLUSTER_BP_DIRECT 1
+#endif
+constexpr Flt CLUSTER_BP = FUFFT_CLUSTER_BP_DIRECT ? Flt::BP_DIRECT : Flt::SMEM;
+
 template<class Inner, int C, int OUT_L, int OUT_SHIFT, bool BFP = false>
 static fufft_status cluster_mid(fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
 {
    switch(mid) {
    case FUFFT_MID_NONE: return launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::NONE, Flt::NONE, BFP>(a, st, dev);
    case FUFFT_MID_MULTIPLY:
-      return bperm ? launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::MUL, Flt::SMEM, BFP>(a, st, dev)
+      return bperm ? launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::MUL, CLUSTER_BP, BFP>(a, st, dev)
                    : launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::MUL, Flt::GLOBAL, BFP>(a, st, dev);
    case FUFFT_MID_CONJ_MULTIPLY:
-      return bperm ? launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::CONJ, Flt::SMEM, BFP>(a, st, dev)
+      return bperm ? launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::CONJ, CLUSTER_BP, BFP>(a, st, dev)
                    : launch_cluster<Inner, C, OUT_L, OUT_SHIFT, Mid::CONJ, Flt::GLOBAL, BFP>(a, st, dev);
    }
    return FUFFT_ERR_INVALID_ARG;

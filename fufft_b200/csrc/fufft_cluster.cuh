@@ -271,6 +271,15 @@ struct ClusterConv {
                if constexpr(BFP) f[k] = bfp_dequant(reinterpret_cast<const uint32_t*>(F)[lane + k * T], sb);
                else f[k] = reinterpret_cast<const float2*>(F)[lane + k * T];
             }
+         } else if constexpr(FLT == Flt::BP_DIRECT) {
+            // the same register-boundary order read coalesced from global
+            // memory: no shared-memory copy, so more CTAs fit on an SM
+#pragma unroll
+            for(int k = 0; k < R; ++k) {
+               if constexpr(BFP)
+                  f[k] = bfp_dequant(__ldg(static_cast<const uint32_t*>(args.b) + fbase + lane + k * T), sb);
+               else f[k] = __ldg(static_cast<const float2*>(args.b) + fbase + lane + k * T);
+            }
          } else if constexpr(BFP) {
             const uint4* fp = reinterpret_cast<const uint4*>(static_cast<const uint32_t*>(args.b) + fbase +
                                                              (size_t)lane * R);
@@ -366,8 +375,15 @@ struct ClusterConv {
    }
 };
 
+// 768 resident threads per SM (three CTAs of 256, six of 128; 80 registers):
+// the load, exchange and compute phases of one cluster barely overlap, so
+// more resident clusters hide them better (+8-20% over 512 on the 1-D,
+// four-step and 2-D shapes; 1024 spills and is slower)
+#ifndef FUFFT_CLUSTER_RESIDENT
+#define FUFFT_CLUSTER_RESIDENT 768
+#endif
 template<class Inner, int C, int OUT_L, int OUT_SHIFT, Mid MID, Flt FLT, bool BFP>
-__global__ void __launch_bounds__(Inner::T, min_blocks<Inner::T>())
+__global__ void __launch_bounds__(Inner::T, min_blocks<Inner::T, FUFFT_CLUSTER_RESIDENT>())
 conv_cluster_kernel(const ConvArgs args)
 {
    ClusterConv<Inner, C, OUT_L, OUT_SHIFT, MID, FLT, BFP>::run(args);

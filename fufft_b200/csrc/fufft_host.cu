@@ -41,11 +41,15 @@ long long chunk_transforms(int n, long long batch)
    return ct < batch ? ct : batch;
 }
 
+#ifndef FUFFT_HOST_TWO_UPLOADS
+#define FUFFT_HOST_TWO_UPLOADS 1
+#endif
 struct Pipe {
    std::mutex mu;
    bool ready = false;
-   cudaStream_t h2d = nullptr, comp = nullptr, d2h = nullptr;
-   cudaEvent_t start = nullptr, up[SLOTS] = {}, done[SLOTS] = {}, down[SLOTS] = {};
+   // h2d2 carries the filters so two copy engines share the upload direction
+   cudaStream_t h2d = nullptr, h2d2 = nullptr, comp = nullptr, d2h = nullptr;
+   cudaEvent_t start = nullptr, up[SLOTS] = {}, up2[SLOTS] = {}, done[SLOTS] = {}, down[SLOTS] = {};
 };
 constexpr int MAX_DEVICES = 64;
 Pipe g_pipe[MAX_DEVICES];
@@ -53,11 +57,11 @@ Pipe g_pipe[MAX_DEVICES];
 fufft_status pipe_init(Pipe& p)
 {
    fufft_status s;
-   for(cudaStream_t* st : {&p.h2d, &p.comp, &p.d2h})
+   for(cudaStream_t* st : {&p.h2d, &p.h2d2, &p.comp, &p.d2h})
       if((s = check(cudaStreamCreateWithFlags(st, cudaStreamNonBlocking))) != FUFFT_OK) return s;
    if((s = check(cudaEventCreateWithFlags(&p.start, cudaEventDisableTiming))) != FUFFT_OK) return s;
    for(int i = 0; i < SLOTS; ++i)
-      for(cudaEvent_t* e : {&p.up[i], &p.done[i], &p.down[i]})
+      for(cudaEvent_t* e : {&p.up[i], &p.up2[i], &p.done[i], &p.down[i]})
          if((s = check(cudaEventCreateWithFlags(e, cudaEventDisableTiming))) != FUFFT_OK) return s;
    p.ready = true;
    return FUFFT_OK;
@@ -124,8 +128,10 @@ fufft_status fufft_conv_c2c_f32_host(const float* a, const float* b, float* out,
    const float* bdev = nullptr;
    // the pipeline starts after the work already queued on the caller's stream
    if((s = check(cudaEventRecord(p.start, st))) != FUFFT_OK) return s;
-   for(cudaStream_t q : {p.h2d, p.comp, p.d2h})
+   for(cudaStream_t q : {p.h2d, p.h2d2, p.comp, p.d2h})
       if((s = check(cudaStreamWaitEvent(q, p.start, 0))) != FUFFT_OK) return s;
+   const bool two = FUFFT_HOST_TWO_UPLOADS && has_filter && filter_stride == n;
+   cudaStream_t fup = two ? p.h2d2 : p.h2d;
    if(has_filter && filter_stride == 0) {
       float* shared = reinterpret_cast<float*>(ws + SLOTS * plan.slot_bytes);
       if((s = check(cudaMemcpyAsync(shared, b, pt, cudaMemcpyHostToDevice, p.h2d))) != FUFFT_OK) return s;
@@ -141,16 +147,19 @@ fufft_status fufft_conv_c2c_f32_host(const float* a, const float* b, float* out,
       const size_t bytes = (size_t)cnt * pt;
       // upload: the slot is free once its previous result has left
       if(i >= SLOTS && (s = check(cudaStreamWaitEvent(p.h2d, p.down[slot], 0))) != FUFFT_OK) return s;
+      if(two && i >= SLOTS && (s = check(cudaStreamWaitEvent(fup, p.down[slot], 0))) != FUFFT_OK) return s;
       if((s = check(cudaMemcpyAsync(sig, a + (size_t)t0 * 2 * n, bytes, cudaMemcpyHostToDevice, p.h2d))) != FUFFT_OK)
          return s;
       if(has_filter && filter_stride == n) {
-         if((s = check(cudaMemcpyAsync(flt, b + (size_t)t0 * 2 * n, bytes, cudaMemcpyHostToDevice, p.h2d))) !=
+         if((s = check(cudaMemcpyAsync(flt, b + (size_t)t0 * 2 * n, bytes, cudaMemcpyHostToDevice, fup))) !=
             FUFFT_OK)
             return s;
       }
       if((s = check(cudaEventRecord(p.up[slot], p.h2d))) != FUFFT_OK) return s;
+      if(two && (s = check(cudaEventRecord(p.up2[slot], fup))) != FUFFT_OK) return s;
       // convolve in place
       if((s = check(cudaStreamWaitEvent(p.comp, p.up[slot], 0))) != FUFFT_OK) return s;
+      if(two && (s = check(cudaStreamWaitEvent(p.comp, p.up2[slot], 0))) != FUFFT_OK) return s;
       s = fufft_conv_c2c_f32(sig, has_filter ? (filter_stride == n ? flt : bdev) : nullptr, sig, n, cnt, layout, mid,
                              has_filter ? filter_stride : n, reinterpret_cast<fufft_stream_t>(p.comp));
       if(s != FUFFT_OK) return s;
