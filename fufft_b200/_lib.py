@@ -62,6 +62,8 @@ SIGNATURES = {
     "fufft_peer_open": (_I, [_P, ct.POINTER(_P)]),
     "fufft_peer_close": (_I, [_P]),
     "fufft_peer_free": (_I, [_P]),
+    "fufft_conv_multi_gpu": (_I, [_P]),
+    "fufft_mg_chain": (_I, [_I64, _I, ct.POINTER(_I)]),
 }
 
 

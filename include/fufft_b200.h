@@ -314,6 +314,68 @@ fufft_status fufft_peer_open(const void* ipc_handle, void** dev_ptr);
 fufft_status fufft_peer_close(void* dev_ptr);
 fufft_status fufft_peer_free(void* dev_ptr);
 
+/* ---- several GPUs from one host thread (new: the reference is single-GPU).
+ * fufft_conv_multi_gpu runs one job over the GPUs of desc->shards.  It
+ * enqueues on every shard's stream and returns without waiting, and it leaves
+ * the caller's current device as it found it.  Modes:
+ *   FUFFT_MG_BATCH: independent transforms.  Shard i convolves its own
+ *     `batch` transforms exactly as fufft_conv_c2c_f32 would, with
+ *     desc->layout / mid / filter_stride.  a, b, out are device memory of
+ *     shard i's GPU.
+ *   FUFFT_MG_BATCH_HOST: the same from pinned host memory.  Shard i runs
+ *     fufft_conv_c2c_f32_host on its GPU with its own workspace
+ *     (fufft_conv_host_workspace bytes on that GPU), so each GPU's PCIe link
+ *     carries its own slice.
+ *   FUFFT_MG_SINGLE_SIGNAL: one n-point convolution over 2, 4 or 8 shards
+ *     (shard index = rank), the scheme of fufft_dist_pass_push / _pull.
+ *     out: this rank's [world][n/world^2] slice of the signal, convolved in
+ *     place (a must be NULL or equal to out).
+ *     b: block `rank` of the filter, n/world points in the order of
+ *     fufft_mg_chain, with 1/n folded in.
+ *     workspace: n/world complex points on the shard's GPU; every rank stores
+ *     into it and later loads from it.
+ *     Distinct GPUs must reach each other by peer access, else
+ *     FUFFT_ERR_PEER_UNAVAILABLE; shards may share a GPU.  Events between the
+ *     shard streams order the phases, so no kernel of one rank waits on the
+ *     device for another rank.
+ * Arguments common to all shards are checked before the first launch.  The
+ * BATCH modes check each shard's pointers when its turn comes; a CUDA error or
+ * a rejected shard returns at once, and work already queued on earlier shards
+ * stays queued. */
+typedef enum fufft_mg_mode {
+   FUFFT_MG_BATCH = 0,
+   FUFFT_MG_BATCH_HOST = 1,
+   FUFFT_MG_SINGLE_SIGNAL = 2
+} fufft_mg_mode;
+typedef struct fufft_mg_shard {
+   int device;              /* CUDA device ordinal */
+   fufft_stream_t stream;   /* a stream of that device (NULL: its legacy default stream) */
+   const float* a;          /* signal (BATCH, BATCH_HOST) */
+   const float* b;          /* filter(s) or the rank's filter block */
+   float* out;              /* result, or the rank's slice (SINGLE_SIGNAL, in place) */
+   int64_t batch;           /* transforms of this shard (BATCH, BATCH_HOST) */
+   void* workspace;         /* BATCH_HOST: pipeline slots; SINGLE_SIGNAL: the rank's block */
+   size_t workspace_bytes;
+} fufft_mg_shard;
+typedef struct fufft_mg_desc {
+   fufft_mg_mode mode;
+   int n_shards;            /* 1..FUFFT_MG_MAX_SHARDS; SINGLE_SIGNAL: 2, 4 or 8 */
+   const fufft_mg_shard* shards;
+   int64_t n;               /* points per transform (SINGLE_SIGNAL: of the one signal) */
+   fufft_layout layout;     /* filter layout (BATCH, BATCH_HOST) */
+   fufft_midop mid;
+   int64_t filter_stride;   /* BATCH, BATCH_HOST: as in fufft_conv_c2c_f32 */
+} fufft_mg_desc;
+#define FUFFT_MG_MAX_SHARDS 64
+fufft_status fufft_conv_multi_gpu(const fufft_mg_desc* desc);
+
+/* Radix chain of the whole n-point transform of FUFFT_MG_SINGLE_SIGNAL over
+ * `world` ranks: [world] followed by the block's chain.  Written to
+ * radices_out (room for 32).  Returns its length, or -1 if the shape is not
+ * supported.  Filter slot p holds spectrum bin
+ * fufft_chain_rev(p, radices, length). */
+int fufft_mg_chain(int64_t n, int world, int* radices_out);
+
 /* The same BFP four-step for callers that cannot allocate device memory when
  * they call the library (a host whose device memory is entirely held by its
  * own pool allocator, or a latency-critical loop where an allocation's
