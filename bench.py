@@ -299,10 +299,10 @@ def run_ncu_all():
     call("conv fp32 R16_BPERM conj-multiply", lambda: ops.conv(a, b, n, ops.LAYOUT_R16_BPERM, ops.MID_CONJ_MULTIPLY, out=o), pts, 24 * pts)
     aq, as_ = ops.bfp_pack(a, n)
     torch.cuda.synchronize()
-    man.append(("bfp_pack: abs-max, quantise, scale kernels", 3, pts, 20 * pts))
+    man.append(("bfp_pack (one pass: abs-max and quantise in one CTA per transform)", 1, pts, 12 * pts + 4 * batch))
     bq, bs = ops.bfp_pack(b, n)
     torch.cuda.synchronize()
-    man.append(("bfp_pack (filter)", 3, pts, 20 * pts))
+    man.append(("bfp_pack (filter)", 1, pts, 12 * pts + 4 * batch))
     call("conv int16-BFP R16", lambda: ops.conv_bfp(aq, as_, bq, bs, n, ops.LAYOUT_R16), pts, 12 * pts + 12 * batch)
     call("conv int16-BFP R16_BPERM", lambda: ops.conv_bfp(aq, as_, bq, bs, n, ops.LAYOUT_R16_BPERM), pts, 12 * pts + 12 * batch)
     call("bfp_unpack", lambda: ops.bfp_unpack(aq, as_, n), pts, 12 * pts)
@@ -340,7 +340,7 @@ def run_ncu_all():
     aq, as_ = ops.bfp_pack(a, n2)
     bq, bs = ops.bfp_pack(b, n2)
     torch.cuda.synchronize()
-    man.append(("bfp_pack x2 (four-step inputs)", 6, 0, 0))
+    man.append(("bfp_pack x2 (four-step inputs, n > 8192: abs-max pass + quantise pass)", 6, 0, 0))
     call("int16-BFP four-step N=32768 cluster C=16",
          lambda: ops.conv_large_bfp(aq, as_, bq, bs, n2, ops.LAYOUT_R16_BPERM, r_out=16, mid_size=2048),
          pts, 12 * pts + 12 * (pts // n2))
@@ -544,9 +544,9 @@ def run_sweep(args):
             emit(f"6: natural-order c2c {name} N={n} batch={batch}", ms, batch * n, 16)
         ms = time_steps(torch, lambda: ops.filter_from_taps(a, n, ops.LAYOUT_R16_BPERM), steps, warm, None)
         emit(f"6: filter from taps N={n} batch={batch} (R16_BPERM)", ms, batch * n, 16)
-        # int16-BFP pack: abs-max pass + quantise pass over fp32 (8 + 8 read, 4 write per point)
+        # int16-BFP pack: one pass for n <= 8192 (8 read, 4 write per point, 4 per scale)
         ms = time_steps(torch, lambda: ops.bfp_pack(a, n), steps, warm, None)
-        emit(f"6: int16-BFP pack N={n} batch={batch} (two passes)", ms, batch * n, 20)
+        emit(f"6: int16-BFP pack N={n} batch={batch} (one pass)", ms, batch * n, 12, 4 * batch)
         del o
         # fused two-for-one real convolution: 2 x 2^27 real points, one real filter
         # spectrum per pair (12 B per real point: 4+4 read, 8 filter per pair slot, 4+4 write)

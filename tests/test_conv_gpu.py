@@ -156,7 +156,8 @@ def test_r2_two_for_one(ops, oracle, key):
     assert rel_l2(_host(ur), want_u) <= F32_TOL and rel_l2(_host(vr), want_v) <= F32_TOL
 
 
-@pytest.mark.parametrize("n", [16, 256, 512, 1024, 2048, 4096, 8192])
+# one-pass kernel: even n <= 8192 (powers of two and not); two passes: odd n, n > 8192
+@pytest.mark.parametrize("n", [2, 16, 256, 512, 1024, 2048, 3000, 4096, 8192, 999, 16384])
 def test_bfp_pack_bit_exact_and_unpack(ops, oracle, n):
     rng = np.random.default_rng(n)
     x = (rng.standard_normal(7 * n) + 1j * rng.standard_normal(7 * n)).astype(np.complex64)
