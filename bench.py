@@ -547,6 +547,11 @@ def run_sweep(args):
         # int16-BFP pack: one pass for n <= 8192 (8 read, 4 write per point, 4 per scale)
         ms = time_steps(torch, lambda: ops.bfp_pack(a, n), steps, warm, None)
         emit(f"6: int16-BFP pack N={n} batch={batch} (one pass)", ms, batch * n, 12, 4 * batch)
+        # int16-BFP unpack: 4 read, 8 write per point, 4 per scale
+        q, qs = ops.bfp_pack(a, n)
+        ms = time_steps(torch, lambda: ops.bfp_unpack(q, qs, n), steps, warm, None)
+        emit(f"6: int16-BFP unpack N={n} batch={batch}", ms, batch * n, 12, 4 * batch)
+        del q, qs
         del o
         # fused two-for-one real convolution: 2 x 2^27 real points, one real filter
         # spectrum per pair (12 B per real point: 4+4 read, 8 filter per pair slot, 4+4 write)
