@@ -544,6 +544,8 @@ def run_sweep(args):
             emit(f"6: natural-order c2c {name} N={n} batch={batch}", ms, batch * n, 16)
         ms = time_steps(torch, lambda: ops.filter_from_taps(a, n, ops.LAYOUT_R16_BPERM), steps, warm, None)
         emit(f"6: filter from taps N={n} batch={batch} (R16_BPERM)", ms, batch * n, 16)
+        ms = time_steps(torch, lambda: ops.filter_permute(a, n, ops.LAYOUT_R16_BPERM), steps, warm, None)
+        emit(f"6: filter permutation of natural spectra N={n} batch={batch} (R16_BPERM)", ms, batch * n, 16)
         # int16-BFP pack: one pass for n <= 8192 (8 read, 4 write per point, 4 per scale)
         ms = time_steps(torch, lambda: ops.bfp_pack(a, n), steps, warm, None)
         emit(f"6: int16-BFP pack N={n} batch={batch} (one pass)", ms, batch * n, 12, 4 * batch)

@@ -249,7 +249,8 @@ __global__ void filter_permute_kernel(const float2* __restrict__ in, float2* __r
 }
 
 // ---------------------------------------------------------------------------
-// int16 BFP pack / unpack.  pack = three short launches so any n works:
+// int16 BFP pack / unpack.  Even n <= 8192: one pass (bfp_pack_onepass_kernel
+// below).  Otherwise three short launches, so any n works:
 //   1) per-transform abs-max into the scale array (atomicMax on the fp32
 //      bits, which order like the values for x >= 0);
 //   2) quantise with inv = 32767 / max(mx, 1e-30);

@@ -104,7 +104,7 @@ def test_conv_broadcast_filter_and_inplace(ops, oracle):
 
 def test_device_filter_permute_bit_exact(ops, oracle):
     rng = np.random.default_rng(1)
-    for n in (64, 512, 2048, 4096):
+    for n in (64, 512, 2048, 4096, 8192):      # shared-memory staged gather (8192: 64 KB)
         b = (rng.standard_normal(3 * n) + 1j * rng.standard_normal(3 * n)).astype(np.complex64)
         for lname, (layout, radix, v) in LAYOUTS.items():
             if n > (4096 if radix == 8 else 8192):
