@@ -248,7 +248,7 @@ def run_ours(args, rank, world, dist):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
                      "traffic": profile_traffic(f"conv_f32_r16_bperm_n{n}"),
-                     "bytes_per_point": BYTES_F32, "kernel": f"conv_kernel<{n},16,...,MUL,SMEM> (1 launch/step)"},
+                     "bytes_per_point": BYTES_F32, "kernel": f"conv_kernel<{n},16,...,MUL,BP_DIRECT> (1 launch/step)"},
         "bfp": {"value": round(gpts_bfp * world, 3), "unit": "Gpoints/s", "ms_per_step": round(ms_bfp, 4),
                 "roofline": {"bound": "hbm", "achieved": round(ach_bfp, 1), "peak": hbm, "unit": "GB/s",
                              "frac": round(ach_bfp / hbm, 4), "bytes_per_point": BYTES_BFP,

@@ -707,7 +707,8 @@ struct ConvKernel {
 // CTAs, up to 128 registers per thread, no spills).  int16-BFP: 1024 (64
 // registers): the BFP kernel moves half the bytes and is bound by issue and
 // latency, and four CTAs per SM measured 10-20% faster at N = 512..4096;
-// fp32 measured 3-9% slower at 768 or 1024.
+// fp32 measured 3-9% slower at 768 or 1024 with the filter tile in shared
+// memory (see resident_for below for the one fp32 case that runs 768).
 #ifndef FUFFT_RESIDENT_THREADS
 #define FUFFT_RESIDENT_THREADS 512
 #endif
@@ -732,8 +733,26 @@ template<In IN, Out OUT> constexpr int resident_threads()
                             : FUFFT_RESIDENT_THREADS;
 }
 
+// 1-D radix-16 fp32 convolution of n >= 2048 with the register-boundary filter read
+// straight from global memory (no 32 KB shared-memory filter tile per CTA):
+// three CTAs of 256 threads per SM at <= 80 registers, no spills.  Against
+// two CTAs with the filter tile: +8-9% at n = 4096, +4-6% at 2048 (B200, 1 GiB
+// batches); at n <= 1024, and for the natural-order kernels, 768 threads
+// measured 2-7% slower, so they keep their targets.
+#ifndef FUFFT_RESIDENT_THREADS_CONV_DIRECT
+#define FUFFT_RESIDENT_THREADS_CONV_DIRECT 768
+#endif
+constexpr int CONV_DIRECT_MIN_N = 2048;
+template<class C, In IN, Out OUT, Flt FLT> constexpr int resident_for()
+{
+   return (IN == In::C32 && OUT == Out::C32 && FLT == Flt::BP_DIRECT && C::H == 1 && C::R == 16 &&
+           C::N >= CONV_DIRECT_MIN_N)
+             ? FUFFT_RESIDENT_THREADS_CONV_DIRECT
+             : resident_threads<IN, OUT>();
+}
+
 template<class C, int CPB, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>
-__global__ void __launch_bounds__(CPB * C::T, min_blocks<CPB * C::T, resident_threads<IN, OUT>()>())
+__global__ void __launch_bounds__(CPB * C::T, min_blocks<CPB * C::T, resident_for<C, IN, OUT, FLT>()>())
 conv_kernel(const ConvArgs args)
 {
    ConvKernel<C, CPB, IN, OUT, MID, FLT, FBFP>::run(args);

@@ -69,7 +69,8 @@ fufft_status launch_chain(const ConvArgs& args, cudaStream_t st, int device)
          // it needs fewer registers than the target allows: a shared-memory
          // carve-out that fits exactly that many CTAs (1 KB reserved per CTA),
          // the rest of the SM's 256 KB stays L1
-         constexpr int ctas = resident_threads<IN, OUT>() >= K::THREADS ? resident_threads<IN, OUT>() / K::THREADS : 1;
+         constexpr int target = resident_for<C, IN, OUT, FLT>();
+         constexpr int ctas = target >= K::THREADS ? target / K::THREADS : 1;
          constexpr long long need = (long long)ctas * ((long long)K::SMEM + 1024);
          const int pct = need >= 228 * 1024 ? 100 : (int)((need * 100 + 228 * 1024 - 1) / (228 * 1024));
          if(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, pct) != cudaSuccess)
@@ -198,9 +199,19 @@ namespace fufft {
 namespace host {
 
 // mid-op / filter-read selection -> instantiation
+// fp32 radix-16 with the register-boundary filter, n >= CONV_DIRECT_MIN_N: the filter
+// read straight from global memory at three CTAs per SM (resident_for)
+#ifndef FUFFT_CONV_FILTER_DIRECT
+#define FUFFT_CONV_FILTER_DIRECT 1
+#endif
 template<int R, In IN, Out OUT, bool FBFP>
 fufft_status dispatch_mid(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
 {
+   if constexpr(FUFFT_CONV_FILTER_DIRECT && R == 16 && !FBFP && IN == In::C32 && OUT == Out::C32) {
+      if(bperm && n >= CONV_DIRECT_MIN_N && mid != FUFFT_MID_NONE)
+         return mid == FUFFT_MID_MULTIPLY ? launch_n<R, IN, OUT, Mid::MUL, Flt::BP_DIRECT, FBFP>(n, a, st, dev)
+                                          : launch_n<R, IN, OUT, Mid::CONJ, Flt::BP_DIRECT, FBFP>(n, a, st, dev);
+   }
    switch(mid) {
    case FUFFT_MID_NONE: return launch_n<R, IN, OUT, Mid::NONE, Flt::NONE, FBFP>(n, a, st, dev);
    case FUFFT_MID_MULTIPLY:
