@@ -733,20 +733,22 @@ template<In IN, Out OUT> constexpr int resident_threads()
                             : FUFFT_RESIDENT_THREADS;
 }
 
-// 1-D radix-16 fp32 convolution of n >= 2048 with the register-boundary filter read
-// straight from global memory (no 32 KB shared-memory filter tile per CTA):
-// three CTAs of 256 threads per SM at <= 80 registers, no spills.  Against
-// two CTAs with the filter tile: +8-9% at n = 4096, +4-6% at 2048 (B200, 1 GiB
-// batches); at n <= 1024, and for the natural-order kernels, 768 threads
-// measured 2-7% slower, so they keep their targets.
+// 1-D radix-16 fp32 convolution (complex or two-for-one real) of n >= 2048
+// with the register-boundary filter read straight from global memory (no
+// 32 KB shared-memory filter tile per CTA): three CTAs of 256 threads per SM
+// at <= 80 registers, no spills.  Against two CTAs with the filter tile:
+// +8-9% at n = 4096 and +4-6% at 2048 for the complex convolution, +6-8% at
+// 4096 for the two-for-one real one (B200, 1 GiB batches).  At n <= 1024,
+// and for the natural-order kernels, 768 threads measured 2-7% slower, so
+// they keep their targets.
 #ifndef FUFFT_RESIDENT_THREADS_CONV_DIRECT
 #define FUFFT_RESIDENT_THREADS_CONV_DIRECT 768
 #endif
 constexpr int CONV_DIRECT_MIN_N = 2048;
 template<class C, In IN, Out OUT, Flt FLT> constexpr int resident_for()
 {
-   return (IN == In::C32 && OUT == Out::C32 && FLT == Flt::BP_DIRECT && C::H == 1 && C::R == 16 &&
-           C::N >= CONV_DIRECT_MIN_N)
+   return (((IN == In::C32 && OUT == Out::C32) || (IN == In::REAL2 && OUT == Out::REAL2)) &&
+           FLT == Flt::BP_DIRECT && C::H == 1 && C::R == 16 && C::N >= CONV_DIRECT_MIN_N)
              ? FUFFT_RESIDENT_THREADS_CONV_DIRECT
              : resident_threads<IN, OUT>();
 }
