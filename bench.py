@@ -293,7 +293,7 @@ def run_ncu_all():
         torch.cuda.synchronize()
         man.append((label, launches, points, nbytes))
 
-    call("conv fp32 R16_BPERM (register-boundary filter, TMA)", lambda: ops.conv(a, b, n, ops.LAYOUT_R16_BPERM, out=o), pts, 24 * pts)
+    call("conv fp32 R16_BPERM (register-boundary filter, read directly)", lambda: ops.conv(a, b, n, ops.LAYOUT_R16_BPERM, out=o), pts, 24 * pts)
     call("conv fp32 R16 (linear filter: pipelined kernel)", lambda: ops.conv(a, b, n, ops.LAYOUT_R16, out=o), pts, 24 * pts)
     call("conv fp32 R8_BPERM", lambda: ops.conv(a, b, n, ops.LAYOUT_R8_BPERM, out=o), pts, 24 * pts)
     call("conv fp32 R16_BPERM conj-multiply", lambda: ops.conv(a, b, n, ops.LAYOUT_R16_BPERM, ops.MID_CONJ_MULTIPLY, out=o), pts, 24 * pts)
