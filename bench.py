@@ -35,6 +35,9 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+# the single-signal record maps peer memory with plain loads and stores; NCCL
+# (barriers and one-element all-reduces only) runs without NVLink multicast
+os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
 
 N = 4096
 POINTS = 1 << 27
@@ -163,6 +166,76 @@ def make_inputs(ops, torch, n, batch, seed, device):
     return a, spec, bperm
 
 
+# ------------------------------------------------------------------------------------------
+# Parity of the buffers a timed loop just produced: float64 DFTs on the device
+# (torch.fft in complex128) as an independent ground truth on the first, the
+# last and 256 seeded-random transforms, outside the timed events.  (The oracle
+# is test infrastructure; the tests compare the same launches with it.)
+def sample_idx(batch, seed, k=256):
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    pick = rng.choice(batch, min(k, batch), replace=False).tolist()
+    return sorted({0, batch - 1, *pick})
+
+
+def rel_l2_t(torch, x, y):
+    x = x.to(torch.complex128)
+    y = y.to(torch.complex128)
+    return float(torch.linalg.vector_norm(x - y) / torch.linalg.vector_norm(y))
+
+
+def natural_rows(ops, torch, rows_chain, radices):
+    """rows in the chain order of `radices` -> natural (frequency) order"""
+    nat = torch.empty_like(rows_chain)
+    nat[:, ops.chain_rev_table(radices, rows_chain.device)] = rows_chain
+    return nat
+
+
+def unbperm_rows(rows, n, v=16):
+    """register-boundary order -> chain order: chain[v*L + k] = bperm[L + k*T]"""
+    return rows.reshape(-1, v, n // v).transpose(1, 2).reshape(-1, n)
+
+
+def conv_f64(torch, a, bnat):
+    """unnormalised IDFT(DFT(a) * b), rows of complex128 (b carries the 1/n)"""
+    return torch.fft.ifft(torch.fft.fft(a) * bnat, norm="forward")
+
+
+def dequant_rows(torch, q, s):
+    """int16 pairs [k, n, 2] and scales [k] -> complex128 [k, n]"""
+    return torch.complex(q[..., 0].double(), q[..., 1].double()) * s.double()[:, None]
+
+
+def parity_f32_1d(ops, torch, a, filt_chain_rows, out, n, batch, idx, radices=None):
+    """fp32 output rows idx against float64; filt_chain_rows(idx) gives the
+    filter rows in chain order"""
+    ii = torch.tensor(idx, device=a.device)
+    want = conv_f64(torch, a.view(batch, n)[ii].to(torch.complex128),
+                    natural_rows(ops, torch, filt_chain_rows(ii), radices or ops.chain(n, 16)).to(torch.complex128))
+    e = rel_l2_t(torch, out.view(batch, n)[ii], want)
+    return {"rel_l2_vs_f64": float(f"{e:.3g}"), "tol": 3e-6, "ok": e < 3e-6, "checked": len(idx)}
+
+
+def parity_bfp_1d(ops, torch, aq, as_, bq, bs, oq, os_, n, batch, idx, radices=None, bperm_v=0):
+    """int16-BFP output rows idx against the exact (float64) convolution of the
+    same quantised inputs; also the mantissas against the exactly rounded BFP
+    result (scale from the exact abs-max, rint(x * 32767 / max))"""
+    ii = torch.tensor(idx, device=aq.device)
+    a64 = dequant_rows(torch, aq.view(batch, n, 2)[ii], as_[ii])
+    b64 = dequant_rows(torch, bq.view(batch, n, 2)[ii], bs[ii])
+    if bperm_v:
+        b64 = unbperm_rows(b64, n, bperm_v)
+    exact = conv_f64(torch, a64, natural_rows(ops, torch, b64, radices or ops.chain(n, 16)))
+    q = oq.view(batch, n, 2)[ii]
+    e = rel_l2_t(torch, dequant_rows(torch, q, os_[ii]), exact)
+    mx = torch.maximum(exact.real.abs().amax(1), exact.imag.abs().amax(1)).clamp_min(1e-30)[:, None]
+    qe = torch.stack([torch.round(exact.real * 32767 / mx), torch.round(exact.imag * 32767 / mx)], -1)
+    dq = (q.double() - qe).abs()
+    return {"rel_l2_vs_f64": float(f"{e:.3g}"), "tol": 6e-5, "ok": e < 6e-5,
+            "max_dq_lsb_vs_exact": int(dq.max()), "mismatch_frac_vs_exact": float(f"{float((dq != 0).double().mean()):.4g}"),
+            "checked": len(idx)}
+
+
 def time_steps(torch, fn, steps, warmup, dist):
     for _ in range(warmup):
         fn()
@@ -184,6 +257,15 @@ def time_steps(torch, fn, steps, warmup, dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     return ms
+
+
+def headline_config(n, batch, world):
+    """the `config` of the headline line (both arms print the same one)"""
+    return {"workload": f"configs[1] fused fp32 cyclic conv N={n}, batch={batch} per GPU "
+                        f"(1 GiB signal), one filter per transform, mid-op multiply, "
+                        f"filter in the radix-16 register-boundary layout",
+            "n": n, "batch_per_gpu": batch, "layout": "R16_BPERM", "parallelism": f"batch-sharded x{world}",
+            "l2": "inputs 3 GiB per step > 126 MB L2 (no flush needed)"}
 
 
 def run_ours(args, rank, world, dist):
@@ -208,15 +290,21 @@ def run_ours(args, rank, world, dist):
     pts = batch * n
     gpts = pts / (ms * 1e-3) / 1e9
     achieved = BYTES_F32 * pts / (ms * 1e-3) / 1e9
+    # the output of the timed launches, checked outside the events
+    idx = sample_idx(batch, 17 + rank)
+    parity = {"fp32": parity_f32_1d(ops, torch, a, lambda ii: unbperm_rows(bperm.view(batch, n)[ii], n),
+                                    out, n, batch, idx)}
 
     # ---- int16 BFP fused conv (same points, the reference's linear filter layout)
     aq, as_ = ops.bfp_pack(a, n)
     bq, bs = ops.bfp_pack(spec, n)
-    ms_bfp = time_steps(torch, lambda: ops.conv_bfp(aq, as_, bq, bs, n, ops.LAYOUT_R16, ops.MID_MULTIPLY),
+    bout = (torch.empty_like(aq), torch.empty(batch, dtype=torch.float32, device=dev))
+    ms_bfp = time_steps(torch, lambda: ops.conv_bfp(aq, as_, bq, bs, n, ops.LAYOUT_R16, ops.MID_MULTIPLY, out=bout),
                         args.steps, args.warmup, dist)
     gpts_bfp = pts / (ms_bfp * 1e-3) / 1e9
     ach_bfp = (BYTES_BFP * pts + 12 * batch) / (ms_bfp * 1e-3) / 1e9
-    del aq, bq
+    parity["bfp"] = parity_bfp_1d(ops, torch, aq, as_, bq, bs, bout[0], bout[1], n, batch, idx)
+    del aq, bq, bout
 
     # ---- e2e through the public API with pinned host buffers: the host-data
     # entry point (fufft_conv_c2c_f32_host) moves signal and filter in and the
@@ -231,6 +319,9 @@ def run_ours(args, rank, world, dist):
         ops.conv_host(ha, hb, ho, n, layout, ops.MID_MULTIPLY, filter_stride=n, workspace=ws)
 
     ms_e2e = time_steps(torch, e2e_step, e2e_steps, 1, dist)
+    # the host-data path runs the same kernel on the same data: bit-identical rows
+    hrows = torch.tensor(idx)
+    parity["e2e_equals_device"] = bool(torch.equal(ho.view(batch, n)[hrows], out.view(batch, n)[hrows.to(dev)].cpu()))
     world_pts = pts * world
     line = {
         "metric": "fused conv Gpoints/s + HBM GB/s (% of B200 peak) at N=4096 fp32 & int16-BFP",
@@ -240,11 +331,7 @@ def run_ours(args, rank, world, dist):
         "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (seeded: signal N(0,1), filter taps U[-1,1) -> spectrum/N)",
-        "config": {"workload": f"configs[1] fused fp32 cyclic conv N={n}, batch={batch} per GPU "
-                               f"(1 GiB signal), one filter per transform, mid-op multiply, "
-                               f"filter in the radix-16 register-boundary layout",
-                   "n": n, "batch_per_gpu": batch, "layout": "R16_BPERM", "parallelism": f"batch-sharded x{world}",
-                   "l2": "inputs 3 GiB per step > 126 MB L2 (no flush needed)"},
+        "config": headline_config(n, batch, world),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
                      "traffic": profile_traffic(f"conv_f32_r16_bperm_n{n}"),
@@ -260,13 +347,221 @@ def run_ours(args, rank, world, dist):
                 "ms_per_step": round(ms_e2e, 3)},
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
+        "parity": parity,
     }
-    del ha, hb, ho
+    del ha, hb, ho, a, spec, bperm, out, ws
+    torch.cuda.empty_cache()
+    if not args.no_configs:
+        line["configs"] = run_configs(args, ops, torch, dist, hbm, rank, world, dev)
+    if world > 1 and not args.no_dist:
+        line["dist"] = run_dist_record(args, ops, torch, dist, rank, world, dev, hbm)
     if rank == 0 and not args.no_cpu_baseline:
         rate, kind, cores, sample = cpu_reference_rate(args.cpu_seconds)
         line["cpu_baseline"] = {"value": round(rate / 1e9, 6), "unit": "Gpoints/s", "cores": cores,
                                 "kind": kind, "sample": sample}
     return line
+
+
+def run_configs(args, ops, torch, dist, hbm, rank, world, dev):
+    """Every BASELINE.json config besides the headline, compactly: per config
+    the whole-job Gpoints/s (every rank runs its own copy: weak scaling, max
+    over ranks), the fraction of the measured HBM peak under its byte model,
+    and the float64 parity of sampled outputs of the timed buffers."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321 + rank)
+    steps, warm = args.steps, args.warmup
+    C = torch.complex64
+
+    def rec(ms, pts, bpp, extra=0, **kw):
+        gbs = (bpp * pts + extra) / (ms * 1e-3) / 1e9
+        return {"value": round(world * pts / (ms * 1e-3) / 1e9, 3), "unit": "Gpoints/s", "ms_per_step": round(ms, 4),
+                "frac": round(gbs / hbm, 4), "bytes_per_point": bpp, **kw}
+
+    res = {}
+    # config 1: N=1024 x 4096 (32 MiB per array: inside L2, so L2 is flushed before every step)
+    n, batch = 1024, 4096
+    a, spec, bperm = make_inputs(ops, torch, n, batch, 1000 * 1 + n + rank, dev)
+    o = torch.empty_like(a)
+    ms = time_flushed(torch, lambda: ops.conv(a, bperm, n, ops.LAYOUT_R16_BPERM, out=o), steps, warm, dist=dist)
+    res["c1_fp32_n1024_b4096"] = rec(ms, batch * n, 24, layout="R16_BPERM", l2="flushed before every step",
+                                     parity=parity_f32_1d(ops, torch, a, lambda ii: unbperm_rows(bperm.view(batch, n)[ii], n),
+                                                          o, n, batch, sample_idx(batch, 1)))
+    del a, spec, bperm, o
+
+    # config 2: the other sizes of the sweep (1 GiB of signal), fp32 and int16-BFP;
+    # at N=4096 also the reference's own linear filter orders (radix-16 and radix-8 chains)
+    for n in (512, 1024, 2048, 4096):
+        batch = POINTS // n
+        a, spec, bperm = make_inputs(ops, torch, n, batch, 1000 * 2 + n + rank, dev)
+        o = torch.empty_like(a)
+        idx = sample_idx(batch, n)
+        if n < 4096:
+            ms = time_steps(torch, lambda: ops.conv(a, bperm, n, ops.LAYOUT_R16_BPERM, out=o), steps, warm, dist)
+            res[f"c2_fp32_n{n}"] = rec(ms, batch * n, 24, layout="R16_BPERM", parity=parity_f32_1d(
+                ops, torch, a, lambda ii: unbperm_rows(bperm.view(batch, n)[ii], n), o, n, batch, idx))
+            aq, as_ = ops.bfp_pack(a, n)
+            bq, bs = ops.bfp_pack(spec, n)
+            bout = (torch.empty_like(aq), torch.empty(batch, dtype=torch.float32, device=dev))
+            ms = time_steps(torch, lambda: ops.conv_bfp(aq, as_, bq, bs, n, ops.LAYOUT_R16, out=bout), steps, warm, dist)
+            res[f"c2_bfp_n{n}"] = rec(ms, batch * n, 12, 12 * batch, layout="R16", parity=parity_bfp_1d(
+                ops, torch, aq, as_, bq, bs, bout[0], bout[1], n, batch, idx))
+            del aq, bq, bout
+        else:
+            del bperm
+            ms = time_steps(torch, lambda: ops.conv(a, spec, n, ops.LAYOUT_R16, out=o), steps, warm, dist)
+            res["c2_fp32_n4096_linear_r16"] = rec(ms, batch * n, 24, layout="R16 (mixedrev16 order)", parity=parity_f32_1d(
+                ops, torch, a, lambda ii: spec.view(batch, n)[ii], o, n, batch, idx))
+            # the radix-8 chain order of the same spectra
+            r8 = ops.chain(n, 8)
+            rev16, rev8 = ops.chain_rev_table(ops.chain(n, 16), dev), ops.chain_rev_table(r8, dev)
+            nat_pos = torch.empty_like(rev16)
+            nat_pos[rev16] = torch.arange(n, device=dev)          # natural bin -> radix-16 chain slot
+            spec = spec.view(batch, n)[:, nat_pos[rev8]].reshape(-1)
+            ms = time_steps(torch, lambda: ops.conv(a, spec, n, ops.LAYOUT_R8, out=o), steps, warm, dist)
+            res["c2_fp32_n4096_linear_r8"] = rec(ms, batch * n, 24, layout="R8 (mixedrev order)", parity=parity_f32_1d(
+                ops, torch, a, lambda ii: spec.view(batch, n)[ii], o, n, batch, idx, r8))
+        del a, spec, o
+
+    # config 3: 1024 real signals x 256 real filters, N=4096: packed pairs -> 512
+    # spectra (once per step) -> every pair x every filter in one launch (4 GiB of
+    # real outputs per mid-op).  Bytes: 4 per real output point + the spectra,
+    # filters and signals read once (they stay in L2)
+    n, nsig, nfilt = 4096, 1024, 256
+    x = torch.randn(nsig * n, device=dev, generator=g)
+    taps = torch.rand(nfilt, n, device=dev, generator=g) * 2 - 1
+    b_nat = torch.fft.fft(taps.double(), dim=1) / n
+    bp = ops.filter_permute(b_nat.to(C).reshape(-1), n, ops.LAYOUT_R16_BPERM)
+    xs = x.view(nsig // 2, 2, n)
+    xr, yr = xs[:, 0].contiguous().view(-1), xs[:, 1].contiguous().view(-1)
+    o = torch.empty(nsig * nfilt * n, device=dev)
+    pairs = [(int(i), int(f)) for i, f in zip(sample_idx(nsig, 3, 32)[:32], sample_idx(nfilt, 4, 32)[:32])]
+    for mid, mname in [(ops.MID_MULTIPLY, "multiply"), (ops.MID_CONJ_MULTIPLY, "conj")]:
+        def step():
+            spec = ops.fwd_r2(xr, yr, n, ops.LAYOUT_R16_BPERM)
+            ops.apply_grid_r2(spec, bp, n, ops.LAYOUT_R16_BPERM, mid, out=o)
+        ms = time_steps(torch, step, steps, warm, dist)
+        si = torch.tensor([p[0] for p in pairs], device=dev)
+        fi = torch.tensor([p[1] for p in pairs], device=dev)
+        bsel = b_nat[fi] if mid == ops.MID_MULTIPLY else b_nat[fi].conj()
+        want = conv_f64(torch, x.view(nsig, n)[si].double().to(torch.complex128), bsel).real
+        got = o.view(nsig, nfilt, n)[si, fi]
+        e = rel_l2_t(torch, got, want)
+        res[f"c3_grid_r2_{mname}"] = rec(ms, nsig * nfilt * n, 4, 8 * n * (nsig // 2 + nfilt) + 16 * n * (nsig // 2),
+                                         unit_points="real output points",
+                                         parity={"rel_l2_vs_f64": float(f"{e:.3g}"), "tol": 3e-6, "ok": e < 3e-6,
+                                                 "checked": len(pairs)})
+    del x, taps, b_nat, bp, xs, xr, yr, o
+
+    # config 4: 2-D 256x256 x 512 images (re U[0,1), im 0), one shared filter:
+    # Gaussian taps, sigma 8 px, centred at (0, 0) with cyclic wrap, plus N(0, 0.01)
+    # noise (0.01 read as the variance)
+    h = w = 256
+    batch = 512
+    a = torch.rand(batch * h * w, device=dev, generator=g).to(C)
+    d = torch.minimum(torch.arange(h, device=dev), h - torch.arange(h, device=dev)).double()
+    gauss = torch.exp(-(d[:, None] ** 2 + d[None, :] ** 2) / (2 * 8.0 ** 2))
+    taps2 = gauss + 0.1 * torch.randn(h, w, device=dev, generator=g).double()
+    b_nat = torch.fft.fft2(taps2) / (h * w)
+    bk = ops.filter_permute2d(b_nat.to(C).reshape(-1), h, w, ops.LAYOUT_R16_BPERM)
+    o = torch.empty_like(a)
+    ms = time_steps(torch, lambda: ops.conv2d(a, bk, h, w, ops.LAYOUT_R16_BPERM, filter_stride=0, out=o), steps, warm,
+                    dist)
+    ii = torch.tensor(sample_idx(batch, 5, 16), device=dev)
+    want = torch.fft.ifft2(torch.fft.fft2(a.view(batch, h, w)[ii].to(torch.complex128)) * b_nat, norm="forward")
+    e = rel_l2_t(torch, o.view(batch, h, w)[ii], want)
+    res["c4_conv2d_256x256_b512"] = rec(ms, batch * h * w, 16, 8 * h * w, layout="R16_BPERM", filter="shared",
+                                        parity={"rel_l2_vs_f64": float(f"{e:.3g}"), "tol": 3e-6, "ok": e < 3e-6,
+                                                "checked": int(ii.numel())})
+    del a, b_nat, bk, o, taps2
+
+    # config 5: four-step N=32768 x 2048, fp32 (cluster kernel, in place: the timed
+    # steps re-convolve the previous result; parity from a fresh run) and int16-BFP
+    n, batch = 32768, 2048
+    r_out, mid = ops.large_plan(n, ops.LAYOUT_R16)
+    lout, q = 0, n // mid
+    while q > 1:
+        q //= r_out
+        lout += 1
+    chain = [r_out] * lout + ops.chain(mid, 16)
+    a = torch.randn(batch * n, dtype=C, device=dev, generator=g)
+    taps = torch.complex(torch.rand(batch * n, device=dev, generator=g) * 2 - 1,
+                         torch.rand(batch * n, device=dev, generator=g) * 2 - 1)
+    b_chain = (torch.fft.fft(taps.view(batch, n)) / n)[:, ops.chain_rev_table(chain, dev)].reshape(-1).contiguous()
+    del taps
+    buf = a.clone()
+    # the fp32 filter in the middle's register-boundary order, chunk by chunk
+    b_bp = b_chain.view(-1, mid // 16, 16).transpose(1, 2).contiguous().view(-1)
+    ms = time_steps(torch, lambda: ops.conv_large(buf, b_bp, n, ops.LAYOUT_R16_BPERM, r_out=r_out, mid_size=mid),
+                    steps, warm, dist)
+    buf.copy_(a)
+    ops.conv_large(buf, b_bp, n, ops.LAYOUT_R16_BPERM, r_out=r_out, mid_size=mid)
+    idx = sample_idx(batch, 6, 64)
+    res["c5_fp32_n32768_b2048"] = rec(ms, batch * n, 24, layout="R16_BPERM", plan=[r_out, mid], parity=parity_f32_1d(
+        ops, torch, a, lambda ii: b_bp.view(batch, n)[ii].reshape(-1, 16, mid // 16).transpose(1, 2).reshape(-1, n),
+        buf, n, batch, idx, chain))
+    del buf, b_bp
+    aq, as_ = ops.bfp_pack(a, n)
+    bq, bs = ops.bfp_pack(b_chain, n)
+    del a, b_chain
+    ws = torch.empty(int(ops.lib().fufft_conv_large_bfp_workspace(n, batch)), dtype=torch.uint8, device=dev)
+    outq = []
+
+    def bstep():
+        outq[:] = ops.conv_large_bfp(aq, as_, bq, bs, n, ops.LAYOUT_R16, r_out=r_out, mid_size=mid, workspace=ws)
+    ms = time_steps(torch, bstep, steps, warm, dist)
+    res["c5_bfp_n32768_b2048"] = rec(ms, batch * n, 12, 12 * batch, layout="R16", plan=[r_out, mid],
+                                     parity=parity_bfp_1d(ops, torch, aq, as_, bq, bs, outq[0], outq[1], n, batch, idx,
+                                                          chain))
+    del aq, bq, ws, outq
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_dist_record(args, ops, torch, dist, rank, world, dev, hbm):
+    """config 5's single signal over the ranks (strong scaling): one N=2^26
+    convolution with the all-to-alls fused into the outer passes as NVLink
+    stores / loads; parity of the same scheme at N=2^20 against float64 on
+    the gathered signal"""
+    from fufft_b200.distributed import (GpuBackend, PeerBlocks, conv_distributed_p2p, filter_block,
+                                        gather_signal, scatter_signal)
+    be = GpuBackend()
+    C = torch.complex64
+    # parity: every rank builds the same global signal and filter
+    ns = 1 << 20
+    plan = be.plan(ns, world)
+    g = torch.Generator(device=dev)
+    g.manual_seed(777)
+    xg = torch.randn(ns, dtype=C, device=dev, generator=g)
+    taps = torch.complex(torch.rand(ns, device=dev, generator=g) * 2 - 1, torch.rand(ns, device=dev, generator=g) * 2 - 1)
+    b_nat = torch.fft.fft(taps.to(torch.complex128)) / ns
+    b_chain = b_nat[ops.chain_rev_table(plan.chain, dev)].to(C)
+    x = scatter_signal(xg, ns, world, rank)
+    peers = PeerBlocks(plan.n_blk)
+    conv_distributed_p2p(x, filter_block(b_chain, ns, world, rank), ns, peers, backend=be, plan=plan)
+    peers.close()
+    parts = [torch.empty(2 * x.numel(), device=dev) for _ in range(world)]
+    dist.all_gather(parts, torch.view_as_real(x).reshape(-1))
+    yg = gather_signal([torch.view_as_complex(p.view(-1, 2)) for p in parts], ns)
+    e = rel_l2_t(torch, yg[None], conv_f64(torch, xg[None].to(torch.complex128), b_nat[None]))
+    del xg, taps, b_nat, b_chain, x, parts, yg
+    # timing: N = 2^26
+    n = 1 << 26
+    plan = be.plan(n, world)
+    g.manual_seed(5000 + rank)
+    x0 = torch.randn(world * plan.cols, dtype=C, device=dev, generator=g)
+    bb = torch.randn(plan.n_blk, dtype=C, device=dev, generator=g) / n
+    peers = PeerBlocks(plan.n_blk)
+    ms = time_steps(torch, lambda: conv_distributed_p2p(x0, bb, n, peers, backend=be, plan=plan), args.steps,
+                    args.warmup, dist)
+    peers.close()
+    nvl = 2 * 8 * plan.n_blk * (world - 1) // world
+    return {"value": round(n / (ms * 1e-3) / 1e9, 3), "unit": "Gpoints/s", "ms_per_step": round(ms, 4),
+            "scaling": "strong", "n": n, "ranks": world,
+            "plan": {"block": plan.n_blk, "r_out": plan.r_out, "mid": plan.mid, "chain": plan.chain},
+            "exchange": "NVLink peer stores / loads fused into the outer passes (no multicast)",
+            "nvlink_bytes_per_gpu": nvl, "nvlink_gbs_per_gpu": round(nvl / (ms * 1e-3) / 1e9, 1),
+            "hbm_frac_per_gpu_24B": round(24 * (n // world) / (ms * 1e-3) / 1e9 / hbm, 4),
+            "parity": {"n": ns, "rel_l2_vs_f64": float(f"{e:.3g}"), "tol": 5e-6, "ok": e < 5e-6}}
 
 
 def run_ncu_all():
@@ -442,7 +737,7 @@ def run_dist(args, rank, world, dist):
                         else "NCCL all_to_all"}}
 
 
-def time_flushed(torch, fn, steps, warmup, flush_bytes=512 << 20):
+def time_flushed(torch, fn, steps, warmup, flush_bytes=512 << 20, dist=None):
     """per-step device time of fn with L2 flushed before every step, outside
     the timed events; for workloads that fit in L2.  The flush writes a
     512 MiB buffer, then reads another 512 MiB one: the write evicts the
@@ -462,7 +757,12 @@ def time_flushed(torch, fn, steps, warmup, flush_bytes=512 << 20):
         e1.record()
         e1.synchronize()
         tot += e0.elapsed_time(e1)
-    return tot / steps
+    ms = tot / steps
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
 
 
 def run_sweep(args):
@@ -636,8 +936,9 @@ def run_reference(args, rank, world):
         "impl": "reference", "value": round(v, 6), "unit": "Gpoints/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"configs[1] fused fp32 cyclic conv N={args.n} on host cores "
-                               "(the reference's CPU transcription kernel_pipeline_v16)", "n": args.n},
+        "config": headline_config(args.n, POINTS // args.n, world),
+        "path": "host cores: the reference's own CPU transcription kernel_pipeline_v16 (verify_kernel.cpp:1051), "
+                "one thread per batch slice",
         "cpu_baseline": {"value": round(v, 6), "unit": "Gpoints/s", "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": round(v, 6), "unit": "Gpoints/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -653,6 +954,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=2.0, help="per-thread CPU baseline sample")
     ap.add_argument("--ref-seconds", type=float, default=1.0, help="per-thread sample per reference step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="headline only (no per-config records)")
+    ap.add_argument("--no-dist", action="store_true", help="under torchrun: no single-signal record")
     ap.add_argument("--ncu-case", nargs="?", const="headline", default=None, choices=["headline", "cluster", "all"],
                     help="one launch per kernel of a group, for ncu")
     ap.add_argument("--dist-mode", choices=["p2p", "nccl"], default="p2p",

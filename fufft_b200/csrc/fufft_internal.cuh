@@ -318,6 +318,12 @@ fufft_status cluster_large_bfp(int r_out, int mid_n, fufft_midop mid, bool bperm
 fufft_status cluster_conv2d(int h, int w, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev);
 bool cluster_conv2d_shape(int h, int w);
 constexpr int MAX_N_CLUSTER = 65536;   // radix-16 layouts, one cluster-fused kernel
+// argument checks of the int16-BFP four-step (fufft_large.cu), shared by its
+// workspace and allocation-free entry points
+fufft_status validate_large_bfp(const int16_t* aq, const float* a_scale, const int16_t* bq, const float* b_scale,
+                                const int16_t* oq, const float* o_scale, int64_t n, int64_t batch, int r_out,
+                                int mid, fufft_layout layout, fufft_midop midop, bool check_workspace,
+                                const void* workspace, size_t workspace_bytes, int* lout, bool* nothing_to_do);
 
 }  // namespace host
 }  // namespace fufft

@@ -235,22 +235,52 @@ size_t fufft_conv_large_bfp_workspace(int64_t n, int64_t batch)
    return n > 0 && batch > 0 ? (size_t)n * (size_t)batch * sizeof(float2) : 0;
 }
 
+}  // extern "C"
+
+namespace fufft {
+namespace host {
+
+// argument checks of the int16-BFP four-step, in the order
+// fufft_conv_large_bfp applies them; the workspace is checked only when
+// check_workspace is set.  FUFFT_OK with *nothing_to_do set: batch 0.
+fufft_status validate_large_bfp(const int16_t* aq, const float* a_scale, const int16_t* bq, const float* b_scale,
+                                const int16_t* oq, const float* o_scale, int64_t n, int64_t batch, int r_out,
+                                int mid, fufft_layout layout, fufft_midop midop, bool check_workspace,
+                                const void* workspace, size_t workspace_bytes, int* lout, bool* nothing_to_do)
+{
+   *nothing_to_do = false;
+   fufft_status s = check_plan(n, r_out, mid, layout, lout);
+   if(s != FUFFT_OK) return s;
+   if(batch < 0 || batch * n > (1LL << 40)) return FUFFT_ERR_INVALID_BATCH;
+   if(batch == 0) {
+      *nothing_to_do = true;
+      return FUFFT_OK;
+   }
+   if(!aq || !a_scale || !oq || !o_scale || (check_workspace && !workspace)) return FUFFT_ERR_INVALID_ARG;
+   if(check_workspace && workspace_bytes < fufft_conv_large_bfp_workspace(n, batch)) return FUFFT_ERR_INVALID_ARG;
+   if((check_workspace && !aligned(workspace, 16)) || !aligned(aq, 4) || !aligned(oq, 4))
+      return FUFFT_ERR_MISALIGNED;
+   if(midop < FUFFT_MID_NONE || midop > FUFFT_MID_CONJ_MULTIPLY) return FUFFT_ERR_INVALID_ARG;
+   if(midop != FUFFT_MID_NONE && (!bq || !b_scale)) return FUFFT_ERR_INVALID_ARG;
+   if(midop != FUFFT_MID_NONE && !aligned(bq, 16)) return FUFFT_ERR_MISALIGNED;
+   return FUFFT_OK;
+}
+
+}  // namespace host
+}  // namespace fufft
+
+extern "C" {
+
 fufft_status fufft_conv_large_bfp(const int16_t* aq, const float* a_scale, const int16_t* bq, const float* b_scale,
                                   int16_t* oq, float* o_scale, int64_t n, int64_t batch, int r_out, int mid,
                                   fufft_layout layout, fufft_midop midop, void* workspace,
                                   size_t workspace_bytes, fufft_stream_t stream)
 {
    int lout = 0;
-   fufft_status s = check_plan(n, r_out, mid, layout, &lout);
-   if(s != FUFFT_OK) return s;
-   if(batch < 0 || batch * n > (1LL << 40)) return FUFFT_ERR_INVALID_BATCH;
-   if(batch == 0) return FUFFT_OK;
-   if(!aq || !a_scale || !oq || !o_scale || !workspace) return FUFFT_ERR_INVALID_ARG;
-   if(workspace_bytes < fufft_conv_large_bfp_workspace(n, batch)) return FUFFT_ERR_INVALID_ARG;
-   if(!aligned(workspace, 16) || !aligned(aq, 4) || !aligned(oq, 4)) return FUFFT_ERR_MISALIGNED;
-   if(midop < FUFFT_MID_NONE || midop > FUFFT_MID_CONJ_MULTIPLY) return FUFFT_ERR_INVALID_ARG;
-   if(midop != FUFFT_MID_NONE && (!bq || !b_scale)) return FUFFT_ERR_INVALID_ARG;
-   if(midop != FUFFT_MID_NONE && !aligned(bq, 16)) return FUFFT_ERR_MISALIGNED;
+   bool nothing = false;
+   fufft_status s = validate_large_bfp(aq, a_scale, bq, b_scale, oq, o_scale, n, batch, r_out, mid, layout, midop,
+                                       true, workspace, workspace_bytes, &lout, &nothing);
+   if(s != FUFFT_OK || nothing) return s;
    DeviceCtx c;
    if((s = device_ctx(&c)) != FUFFT_OK) return s;
    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

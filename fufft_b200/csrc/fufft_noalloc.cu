@@ -12,16 +12,25 @@
 //
 // Limits and behaviour:
 //   * the scratch is FUFFT_NOALLOC_SCRATCH_BYTES (16 MiB) on every GPU that
-//     loads the library, held until the process exits; requests needing more
-//     (8 * n * batch bytes) are rejected with FUFFT_ERR_INVALID_SIZE;
+//     loads the library, held until the process exits; every request whose
+//     8 * n * batch bytes exceed it is rejected with FUFFT_ERR_INVALID_SIZE,
+//     also the one-outer-level radix-16 plans that run as one cluster kernel
+//     without touching the scratch (the limit depends on the sizes only);
+//   * arguments are checked in the same order, with the same status codes,
+//     as fufft_conv_large_bfp; the scratch limit comes after those checks;
 //   * all calls on a device share the one array, so calls that may overlap on
 //     the GPU (different streams without ordering between them) race on it --
 //     serialise them on one stream;
-//   * the first call on each device looks up the array's device address
-//     (cudaGetSymbolAddress, with that device current) and remembers it; make
-//     that first call before any stream capture;
-//   * nothing in the array needs to start at zero: every workspace element is
-//     written by the first outer pass before anything reads it.
+//   * the first successful call on each device looks up the array's device
+//     address (cudaGetSymbolAddress, with that device current) and remembers
+//     it; make that first call before any stream capture.  A lookup that
+//     fails is not remembered: the next call tries again.  The remembered
+//     address belongs to the device's current context; after cudaDeviceReset
+//     the library must be reloaded before this entry point is used again;
+//   * the array keeps the previous call's contents, and nothing in it needs
+//     to start at zero: the first outer pass writes every workspace element
+//     before anything reads it (the per-transform abs-max that must start at
+//     zero lives in the caller's o_scale, cleared on the stream).
 // No cudaMalloc, cudaFree or allocating library routine is called.
 #include <mutex>
 
@@ -31,26 +40,27 @@ namespace {
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[FUFFT_NOALLOC_SCRATCH_BYTES];
 
-struct ScratchSlot {
-   std::once_flag once;
-   void* ptr = nullptr;
-   cudaError_t err = cudaSuccess;
-};
 constexpr int MAX_DEVICES = 64;
-ScratchSlot g_slots[MAX_DEVICES];
+std::mutex g_scratch_mutex;
+void* g_scratch_ptr[MAX_DEVICES] = {};   // device address per device, once looked up
 
 // the host-side name of the array is not a device address: look the address
-// up once per device, with that device current
+// up with the device current, and remember it only once the lookup succeeded
 fufft_status scratch_of_current_device(void** out)
 {
    int dev = 0;
    const cudaError_t e = cudaGetDevice(&dev);
    if(e != cudaSuccess) return fufft::host::cuda_fail(e);
    if(dev < 0 || dev >= MAX_DEVICES) return FUFFT_ERR_UNSUPPORTED;
-   ScratchSlot& s = g_slots[dev];
-   std::call_once(s.once, [&] { s.err = cudaGetSymbolAddress(&s.ptr, g_noalloc_scratch); });
-   if(s.err != cudaSuccess) return fufft::host::cuda_fail(s.err);
-   *out = s.ptr;
+   std::lock_guard<std::mutex> lock(g_scratch_mutex);
+   if(!g_scratch_ptr[dev]) {
+      void* p = nullptr;
+      const cudaError_t le = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if(le != cudaSuccess) return fufft::host::cuda_fail(le);
+      if(!p) return FUFFT_ERR_CUDA;
+      g_scratch_ptr[dev] = p;
+   }
+   *out = g_scratch_ptr[dev];
    return FUFFT_OK;
 }
 
@@ -61,11 +71,14 @@ extern "C" fufft_status fufft_conv_large_bfp_noalloc(const int16_t* aq, const fl
                                                      int64_t batch, int r_out, int mid, fufft_layout layout,
                                                      fufft_midop mid_op, fufft_stream_t stream)
 {
-   if(n <= 0 || batch < 0) return batch < 0 ? FUFFT_ERR_INVALID_BATCH : FUFFT_ERR_INVALID_SIZE;
+   int lout = 0;
+   bool nothing = false;
+   fufft_status s = fufft::host::validate_large_bfp(aq, a_scale, bq, b_scale, oq, o_scale, n, batch, r_out, mid,
+                                                    layout, mid_op, false, nullptr, 0, &lout, &nothing);
+   if(s != FUFFT_OK || nothing) return s;
    if(fufft_conv_large_bfp_workspace(n, batch) > FUFFT_NOALLOC_SCRATCH_BYTES) return FUFFT_ERR_INVALID_SIZE;
    void* scratch = nullptr;
-   const fufft_status s = scratch_of_current_device(&scratch);
-   if(s != FUFFT_OK) return s;
+   if((s = scratch_of_current_device(&scratch)) != FUFFT_OK) return s;
    return fufft_conv_large_bfp(aq, a_scale, bq, b_scale, oq, o_scale, n, batch, r_out, mid, layout, mid_op, scratch,
                                FUFFT_NOALLOC_SCRATCH_BYTES, stream);
 }

@@ -30,7 +30,7 @@ from ._lib import (LAYOUT_NATURAL, LAYOUT_R8, LAYOUT_R8_BPERM, LAYOUT_R16, LAYOU
 __all__ = [
     "MID_NONE", "MID_MULTIPLY", "MID_CONJ_MULTIPLY",
     "LAYOUT_R8", "LAYOUT_R8_BPERM", "LAYOUT_R16", "LAYOUT_R16_BPERM", "LAYOUT_NATURAL",
-    "FufftError", "chain", "chain_rev", "filter_permute", "filter_permute_host", "filter_permute2d", "conv",
+    "FufftError", "chain", "chain_rev", "chain_rev_table", "filter_permute", "filter_permute_host", "filter_permute2d", "conv",
     "conv2d", "fwd", "apply",
     "conv_r2", "bfp_pack", "bfp_unpack", "conv_bfp", "pipeline_ip", "pipeline_fused", "pipeline_v16",
     "pipeline_v16f", "pipeline_r16", "pipeline_fwd", "pipeline_apply", "pipeline_v16_bfp", "init",
@@ -106,6 +106,24 @@ def chain(n: int, radix: int) -> list[int]:
 def chain_rev(idx: int, radices) -> int:
     arr = (ct.c_int * len(radices))(*radices)
     return int(lib().fufft_chain_rev(idx, arr, len(radices)))
+
+
+def chain_rev_table(radices, device=None) -> torch.Tensor:
+    """natural (frequency) index of every chain position of the radix chain
+    `radices` (pass 0 first), as an int64 tensor: the digits of p, pass 0 most
+    significant, written back in reverse order -- fufft_chain_rev for all p at
+    once (verify_kernel.cpp:460-477 chain_rev)"""
+    n = 1
+    for r in radices:
+        n *= int(r)
+    p = torch.arange(n, dtype=torch.int64, device=device)
+    out = torch.zeros_like(p)
+    rest, op = n, 1          # weight of the current digit in p; in the output
+    for r in radices:
+        rest //= int(r)
+        out += ((p // rest) % int(r)) * op
+        op *= int(r)
+    return out
 
 
 def filter_permute(spec_natural: torch.Tensor, n: int, layout: int) -> torch.Tensor:
@@ -331,10 +349,12 @@ def bfp_unpack(q: torch.Tensor, s: torch.Tensor, n: int) -> torch.Tensor:
 
 
 def conv_bfp(aq: torch.Tensor, a_scale: torch.Tensor, bq: torch.Tensor | None, b_scale: torch.Tensor | None,
-             n: int, layout: int = LAYOUT_R16, mid: int = MID_MULTIPLY, filter_stride: int | None = None):
+             n: int, layout: int = LAYOUT_R16, mid: int = MID_MULTIPLY, filter_stride: int | None = None,
+             out: tuple[torch.Tensor, torch.Tensor] | None = None):
+    """int16-BFP fused convolution; out = (oq, o_scale) to reuse output buffers"""
     batch = _batch(aq, n, 2)
-    oq = torch.empty_like(aq)
-    os_ = torch.empty(batch, dtype=torch.float32, device=aq.device)
+    oq, os_ = out if out is not None else (torch.empty_like(aq),
+                                           torch.empty(batch, dtype=torch.float32, device=aq.device))
     fs = n if filter_stride is None else filter_stride
     check(lib().fufft_conv_c2c_bfp(_ptr(aq), _ptr(a_scale), _ptr(bq), _ptr(b_scale), _ptr(oq), _ptr(os_), n,
                                    batch, layout, mid, fs, _stream()), "fufft_conv_c2c_bfp")

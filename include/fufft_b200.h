@@ -383,10 +383,13 @@ int fufft_mg_chain(int64_t n, int world, int* radices_out);
  * the reference.  Instead of a caller workspace it uses a fixed scratch area
  * of FUFFT_NOALLOC_SCRATCH_BYTES that the library reserves on every GPU that
  * loads it (held until exit): 8 * n * batch must not exceed it, else
- * FUFFT_ERR_INVALID_SIZE.  All calls on a device share that area, so calls
- * that may overlap on the GPU race -- keep them on one stream.  The first call
- * on a device looks up the area's address; make it before any stream capture.
- * Allocates nothing. */
+ * FUFFT_ERR_INVALID_SIZE -- for every request, including the one-outer-level
+ * radix-16 plans that would not touch the area.  Other arguments are checked
+ * first, in the order and with the status codes of fufft_conv_large_bfp.  All
+ * calls on a device share that area, so calls that may overlap on the GPU
+ * race -- keep them on one stream.  The first successful call on a device
+ * looks up the area's address (a failed lookup is retried by the next call);
+ * make it before any stream capture.  Allocates nothing. */
 #define FUFFT_NOALLOC_SCRATCH_BYTES (16u << 20)
 fufft_status fufft_conv_large_bfp_noalloc(const int16_t* aq, const float* a_scale, const int16_t* bq,
                                           const float* b_scale, int16_t* oq, float* o_scale, int64_t n,

@@ -48,3 +48,16 @@ def test_host_permutation_matches_oracle(oracle):
             assert np.array_equal(ops.filter_permute_host(b, n, layout), want)
             for i in range(0, n, max(1, n // 64)):
                 assert ops.chain_rev(i, ops.chain(n, radix)) == oracle.chain_rev(i, oracle.chain(n, radix))
+
+
+def test_chain_rev_table_matches_oracle(oracle):
+    """the vectorised digit-reversal table equals the oracle's chain_rev for
+    one-kernel chains, four-step chains and the distributed chain"""
+    import numpy as np
+    from fufft_b200 import ops
+    chains = [ops.chain(n, r) for n, r in [(512, 16), (2048, 8), (4096, 16), (8192, 16)]]
+    chains += [oracle.foursteps_chain(32768, 16, 2048, 16), [8, 16, 16, 16]]
+    for ch in chains:
+        n = int(np.prod(ch))
+        got = ops.chain_rev_table(ch).numpy()
+        assert np.array_equal(got, oracle.rev_table(ch, n)), ch
