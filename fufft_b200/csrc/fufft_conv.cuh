@@ -331,6 +331,9 @@ __device__ __forceinline__ float2 bfp_dequant(uint32_t w, float scale)
 __device__ __forceinline__ uint32_t bfp_quant(float2 v, float inv)
 {
 #if FUFFT_BFP_MAGIC_Q
+   // scalar intrinsics on purpose: a packed f32x2 product followed by a packed
+   // add may be fused into one f32x2 FMA by the assembler, which skips the
+   // product's rounding and breaks bit-exactness with the reference quantiser
    const float fx = __fadd_rn(__fmul_rn(v.x, inv), 12582912.0f);
    const float fy = __fadd_rn(__fmul_rn(v.y, inv), 12582912.0f);
    return __byte_perm(__float_as_uint(fx), __float_as_uint(fy), 0x5410);
@@ -564,7 +567,6 @@ struct ConvKernel {
          static_assert(C::NPC == 0, "natural-order output of 1-D chains");
          sched_fence();
          slot_sync<T, CPB>(slot);   // every thread is past its last read of X
-#pragma unroll
          {
             const int nl = off + lane_natural<C>(lane);
             if constexpr(T % SwzEngine::PERIOD == 0) {

@@ -39,6 +39,16 @@ __device__ __forceinline__ float2 csub(float2 a, float2 b)
        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
    return r;
 }
+// lane-wise product of two fp32 pairs (mul.rn.f32x2: one instruction, each
+// lane rounded as the scalar product)
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b)
+{
+   float2 r;
+   asm("{\n\t.reg .b64 ra, rb, rr;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+       "mul.rn.f32x2 rr, ra, rb;\n\tmov.b64 {%0, %1}, rr;\n\t}"
+       : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+   return r;
+}
 // a * w, two fused products (same rounding shape as the reference's cmul,
 // fufft.cuh:243-261)
 __device__ __forceinline__ float2 cmul(float2 a, float2 w)
@@ -61,17 +71,19 @@ template<int S> __device__ __forceinline__ float2 rot4(float2 a)
 {
    return S < 0 ? make_float2(a.y, -a.x) : make_float2(-a.y, a.x);
 }
-// a * W_8^1 = a * (1 + S i)/sqrt2 : two adds, two multiplies
+// a * W_8^1 = a * (1 + S i)/sqrt2 : two adds, one packed multiply (the
+// assembler may fuse that multiply into the butterfly add that consumes it:
+// one rounding fewer, same or better accuracy)
 template<int S> __device__ __forceinline__ float2 rot8(float2 a)
 {
-   return S < 0 ? make_float2(FUFFT_K_R2 * (a.x + a.y), FUFFT_K_R2 * (a.y - a.x))
-                : make_float2(FUFFT_K_R2 * (a.x - a.y), FUFFT_K_R2 * (a.x + a.y));
+   return S < 0 ? fmul2(make_float2(a.x + a.y, a.y - a.x), make_float2(FUFFT_K_R2, FUFFT_K_R2))
+                : fmul2(make_float2(a.x - a.y, a.x + a.y), make_float2(FUFFT_K_R2, FUFFT_K_R2));
 }
 // a * W_8^3 = a * (-1 + S i)/sqrt2
 template<int S> __device__ __forceinline__ float2 rot8_3(float2 a)
 {
-   return S < 0 ? make_float2(FUFFT_K_R2 * (a.y - a.x), -FUFFT_K_R2 * (a.x + a.y))
-                : make_float2(-FUFFT_K_R2 * (a.x + a.y), FUFFT_K_R2 * (a.x - a.y));
+   return S < 0 ? fmul2(make_float2(a.y - a.x, a.x + a.y), make_float2(FUFFT_K_R2, -FUFFT_K_R2))
+                : fmul2(make_float2(a.x + a.y, a.x - a.y), make_float2(-FUFFT_K_R2, FUFFT_K_R2));
 }
 // a * W_16^e for the exponents the 4x4 radix-16 needs
 template<int E, int S> __device__ __forceinline__ float2 rot16(float2 a)
