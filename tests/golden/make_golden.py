@@ -2,7 +2,7 @@
 
 Run here, where the reference tree exists (it is absent on GPU boxes):
 
-    make -C oracle && python tests/golden/make_golden.py
+    make -C oracle REF_DIR=<reference tree> && python tests/golden/make_golden.py
 
 The reference's tests keep no golden files: their goldens are seeded input
 generators plus fp64 references (verify_kernel.cpp).  This script replays
