@@ -36,7 +36,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 # the single-signal record maps peer memory with plain loads and stores; NCCL
-# (barriers and one-element all-reduces only) runs without NVLink multicast
+# (barriers and one-element all-reduces only) runs with NVLS switched off
 os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
 
 N = 4096
@@ -558,7 +558,7 @@ def run_dist_record(args, ops, torch, dist, rank, world, dev, hbm):
     return {"value": round(n / (ms * 1e-3) / 1e9, 3), "unit": "Gpoints/s", "ms_per_step": round(ms, 4),
             "scaling": "strong", "n": n, "ranks": world,
             "plan": {"block": plan.n_blk, "r_out": plan.r_out, "mid": plan.mid, "chain": plan.chain},
-            "exchange": "NVLink peer stores / loads fused into the outer passes (no multicast)",
+            "exchange": "NVLink peer stores / loads fused into the outer passes (plain peer accesses)",
             "nvlink_bytes_per_gpu": nvl, "nvlink_gbs_per_gpu": round(nvl / (ms * 1e-3) / 1e9, 1),
             "hbm_frac_per_gpu_24B": round(24 * (n // world) / (ms * 1e-3) / 1e9 / hbm, 4),
             "parity": {"n": ns, "rel_l2_vs_f64": float(f"{e:.3g}"), "tol": 5e-6, "ok": e < 5e-6}}
