@@ -2,7 +2,8 @@
 
 ``Oracle`` wraps liboracle.so (the C restatement in fufft_oracle.c);
 ``Reference`` wraps _ref/libfufft_ref.so (the reference's own transcription,
-compiled from its sources by the Makefile here).  Only tests/,
+compiled from its sources by the Makefile here); ``CpuPrograms`` wraps
+_ref/libfufft_cpuref.so (its three CPU programs, the same way).  Only tests/,
 ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg import this module;
 the product library never does.
 
@@ -452,6 +453,83 @@ class Reference:
         b = np.empty(n * batch, np.complex64)
         self.L.ref_gen_large_cfg(n, batch, r_out, mid, _ptr(a), _ptr(b))
         return a, b
+
+
+class CpuPrograms:
+    """The reference's three CPU programs (cpu_fufft.cpp, cpu_inplace.cpp,
+    cpu_mixed.cpp), compiled from its sources through cpuref/ into
+    _ref/libfufft_cpuref.so.  Complex arrays in and out are complex128."""
+
+    SO = os.path.join(HERE, "_ref", "libfufft_cpuref.so")
+
+    def __init__(self) -> None:
+        if not os.path.exists(self.SO):
+            raise FileNotFoundError(self.SO)
+        L = ct.CDLL(self.SO)
+        i = ct.c_int
+        sig = {
+            "ref_cpufufft_main": (i, []), "ref_inplace_main": (i, []), "ref_mixed_main": (i, []),
+            "ref_cpufufft_gen_conv": (None, [i, _P, _P]),
+            "ref_cpufufft_conv": (None, [i, i, _P, _P, _P]),
+            "ref_cpufufft_forward": (None, [i, i, _P, _P]),
+            "ref_inplace_digitrev8": (i, [i, i]),
+            "ref_inplace_conv": (None, [i, i, _P, _P, _P, _P]),
+            "ref_mixed_factorise": (i, [i, i, _P]),
+            "ref_mixed_rev": (i, [i, _P, i]),
+            "ref_mixed_conv": (i, [i, i, _P, _P, _P, _P]),
+        }
+        for name, (res, args) in sig.items():
+            f = getattr(L, name)
+            f.restype, f.argtypes = res, args
+        self.L = L
+
+    @staticmethod
+    def _c128(x) -> np.ndarray:
+        return np.ascontiguousarray(x, dtype=np.complex128)
+
+    def fufft_gen_conv(self, n: int):
+        """check_convolution(n)'s seeded inputs (cpu_fufft.cpp:214-218)"""
+        a, b = np.empty(n, np.complex128), np.empty(n, np.complex128)
+        self.L.ref_cpufufft_gen_conv(n, _ptr(a), _ptr(b))
+        return a, b
+
+    def fufft_conv(self, a, b, n: int, fp32: bool = False) -> np.ndarray:
+        a, b = self._c128(a), self._c128(b)
+        out = np.empty(n, np.complex128)
+        self.L.ref_cpufufft_conv(n, int(fp32), _ptr(a), _ptr(b), _ptr(out))
+        return out
+
+    def fufft_forward(self, x, n: int, fp32: bool = False) -> np.ndarray:
+        x = self._c128(x)
+        out = np.empty(n, np.complex128)
+        self.L.ref_cpufufft_forward(n, int(fp32), _ptr(x), _ptr(out))
+        return out
+
+    def inplace_conv(self, a, b, n: int, fp32: bool = False):
+        """(digit-reversed filter spectrum / n, convolution)"""
+        a, b = self._c128(a), self._c128(b)
+        bs, out = np.empty(n, np.complex128), np.empty(n, np.complex128)
+        self.L.ref_inplace_conv(n, int(fp32), _ptr(a), _ptr(b), _ptr(bs), _ptr(out))
+        return bs, out
+
+    def digitrev8(self, i: int, s: int) -> int:
+        return int(self.L.ref_inplace_digitrev8(i, s))
+
+    def mixed_factorise(self, n: int, v: int) -> list[int]:
+        r = np.zeros(16, np.int32)
+        p = self.L.ref_mixed_factorise(n, v, _ptr(r))
+        return [int(x) for x in r[:p]]
+
+    def mixed_rev(self, i: int, radices) -> int:
+        r = np.ascontiguousarray(radices, dtype=np.int32)
+        return int(self.L.ref_mixed_rev(i, _ptr(r), len(r)))
+
+    def mixed_conv(self, a, b, n: int, v: int):
+        """(chain-order filter spectrum / n, convolution)"""
+        a, b = self._c128(a), self._c128(b)
+        bs, out = np.empty(n, np.complex128), np.empty(n, np.complex128)
+        assert self.L.ref_mixed_conv(n, v, _ptr(a), _ptr(b), _ptr(bs), _ptr(out)) > 0
+        return bs, out
 
 
 def rel_l2(x, y) -> float:

@@ -9,6 +9,7 @@ match the recorded SHA-256 digests bit for bit.
 import hashlib
 import json
 import os
+import sys
 
 import numpy as np
 import pytest
@@ -170,3 +171,70 @@ def test_oracle_c2c_pinned_to_reference(oracle, n):
         assert rel_l2(back, a) <= 2e-6
     f64 = np.fft.fft(a.astype(np.complex128).reshape(batch, n), axis=1).ravel()
     assert rel_l2(want, f64) <= 2e-6
+
+
+# ---- the reference's three CPU programs (cpu_fufft.cpp, cpu_inplace.cpp, cpu_mixed.cpp) ----
+def _cpu_programs():
+    from oracle.oracle import CpuPrograms
+    try:
+        return CpuPrograms()
+    except (FileNotFoundError, OSError):
+        pytest.skip("oracle/_ref/libfufft_cpuref.so not built (needs the reference tree)")
+
+
+def test_cpu_program_fixtures_are_the_programs_outputs():
+    """tests/golden/cpu_programs.npz holds what the compiled programs produce:
+    the digests of their fp64 outputs on the recorded inputs match"""
+    import hashlib
+    import json
+    import os
+    sys_path = os.path.join(os.path.dirname(__file__), "golden")
+    sys.path.insert(0, sys_path)
+    try:
+        import make_cpu_programs as mk
+    finally:
+        sys.path.remove(sys_path)
+    p = _cpu_programs()
+    with open(os.path.join(sys_path, "cpu_programs_digests.json")) as f:
+        dig = json.load(f)
+    assert all(rc == 0 for rc in dig["programs"].values())
+    g = np.load(os.path.join(sys_path, "cpu_programs.npz"))
+    for key, rec in mk.cases(p):
+        for k, v in rec.items():
+            if k in dig[key]:
+                assert hashlib.sha256(np.ascontiguousarray(v).tobytes()).hexdigest() == dig[key][k], (key, k)
+            assert np.array_equal(g[f"{key}/{k}"], v.astype(np.complex64)), (key, k)   # the stored arrays
+
+
+def test_cpu_program_index_maps_bit_exact():
+    """the digit reversal of cpu_inplace and the mixed-radix reversal and
+    factorisation of cpu_mixed equal the library's chain and chain_rev for every
+    index (the filter layouts R8 / R16)"""
+    from fufft_b200 import ops
+    p = _cpu_programs()
+    for n in (8, 64, 512, 4096):
+        s = {8: 1, 64: 2, 512: 3, 4096: 4}[n]
+        want = np.array([p.digitrev8(i, s) for i in range(n)])
+        assert np.array_equal(ops.chain_rev_table(ops.chain(n, 8)).numpy(), want), n
+    for v in (8, 16):
+        for n in (16, 32, 64, 128, 256, 512, 1024, 2048, 4096):
+            if n < v:
+                continue
+            rad = p.mixed_factorise(n, v)
+            assert rad == ops.chain(n, v), (n, v)
+            want = np.array([p.mixed_rev(i, rad) for i in range(n)])
+            assert np.array_equal(ops.chain_rev_table(rad).numpy(), want), (n, v)
+
+
+def test_cpu_program_outputs_agree_with_fp64():
+    """sanity of the fixtures: the programs' convolutions equal a float64
+    numpy convolution of the same inputs"""
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "cpu_programs.npz"))
+    keys = sorted({k.rsplit("/", 1)[0] for k in g.files})
+    for key in keys:
+        a, b = g[key + "/a"].astype(np.complex128), g[key + "/b"].astype(np.complex128)
+        want = np.fft.ifft(np.fft.fft(a) * np.fft.fft(b))
+        for out in ("conv64", "out64", "conv32", "out32"):
+            if f"{key}/{out}" in g.files:
+                assert rel_l2(g[f"{key}/{out}"], want) < (1e-6 if out.endswith("32") else 1e-7), (key, out)
