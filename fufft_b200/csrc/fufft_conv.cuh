@@ -40,8 +40,9 @@ enum class Out { C32, BFP, REAL2, SPEC, SPEC_BP, NAT };
 enum class Mid { NONE, MUL, CONJ };        // pointwise operation between the transforms
 // filter read: register-boundary layout staged by a TMA bulk copy (SMEM) or
 // read straight from global memory (BP_DIRECT: coalesced, no shared memory),
-// or chain order straight from global memory (GLOBAL)
-enum class Flt { NONE, SMEM, GLOBAL, BP_DIRECT };
+// or chain order straight from global memory (GLOBAL), or chain order staged
+// warp by warp through the free part of the exchange buffer (LIN_STAGED)
+enum class Flt { NONE, SMEM, GLOBAL, BP_DIRECT, LIN_STAGED };
 
 __host__ __device__ constexpr int ilog2c(long long n) { return n <= 1 ? 0 : 1 + ilog2c(n / 2); }
 
@@ -614,6 +615,35 @@ struct ConvKernel {
                const float2* fb = static_cast<const float2*>(args.b) + (size_t)filter_off(args, tr) + lane;
 #pragma unroll
                for(int k = 0; k < R; ++k) f[k] = active ? __ldg(fb + k * T) : make_float2(0.f, 0.f);
+            } else if constexpr(FLT == Flt::LIN_STAGED) {
+               // Chain-order filter (the reference's mixedrev16 layout): thread
+               // lane needs the 16 consecutive values at 16*lane.  The last
+               // exchange of each direction is warp-local, so between the last
+               // forward read and the first inverse write this warp's 512
+               // exchange slots [off + 512 w, + 512) belong to it alone: the
+               // warp stages its 512 consecutive filter values there with
+               // coalesced 16-byte loads, then reads its rows back.  16-byte
+               // slot q sits at q ^ ((q >> 3) & 7): conflict-free both ways.
+               static_assert(!FBFP && R == 16 && T >= 32 && C::H == 1, "1-D radix-16 fp32, n >= 512");
+               static_assert(warp_local_exchange<C, C::NP - 2>(), "warp-local last exchange");
+               const int w = lane >> 5, l = lane & 31;
+               float4* S = reinterpret_cast<float4*>(X + off + 512 * w);
+               const float4* src = reinterpret_cast<const float4*>(static_cast<const float2*>(args.b) +
+                                                                  (size_t)filter_off(args, tr) + 512 * w);
+               __syncwarp();                 // every lane is past its last forward read
+#pragma unroll
+               for(int i = 0; i < 8; ++i) {
+                  const float4 v = active ? __ldg(src + l + 32 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                  S[32 * i + (l ^ (((l >> 3) + 4 * i) & 7))] = v;
+               }
+               __syncwarp();
+#pragma unroll
+               for(int i = 0; i < 8; ++i) {
+                  const float4 v = S[8 * l + (i ^ (l & 7))];
+                  f[2 * i] = make_float2(v.x, v.y);
+                  f[2 * i + 1] = make_float2(v.z, v.w);
+               }
+               __syncwarp();                 // before the first inverse exchange reuses the slots
             } else if constexpr(FLT == Flt::SMEM) {
                mbar_wait(&fbar, 0, args.status);
                if constexpr(FBFP) {
@@ -750,7 +780,7 @@ constexpr int CONV_DIRECT_MIN_N = 2048;
 template<class C, In IN, Out OUT, Flt FLT> constexpr int resident_for()
 {
    return (((IN == In::C32 && OUT == Out::C32) || (IN == In::REAL2 && OUT == Out::REAL2)) &&
-           FLT == Flt::BP_DIRECT && C::H == 1 && C::R == 16 && C::N >= CONV_DIRECT_MIN_N)
+           (FLT == Flt::BP_DIRECT || FLT == Flt::LIN_STAGED) && C::H == 1 && C::R == 16 && C::N >= CONV_DIRECT_MIN_N)
              ? FUFFT_RESIDENT_THREADS_CONV_DIRECT
              : resident_threads<IN, OUT>();
 }
