@@ -624,22 +624,26 @@ struct ConvKernel {
                // warp stages its 512 consecutive filter values there with
                // coalesced 16-byte loads, then reads its rows back.  16-byte
                // slot q sits at q ^ ((q >> 3) & 7): conflict-free both ways.
-               static_assert(!FBFP && R == 16 && T >= 32 && C::H == 1, "1-D radix-16 fp32, n >= 512");
+               // (Radix 8: 256 values per warp, the same swizzle; each quarter-warp
+               // of the row reads covers 8 distinct 16-byte bank groups.)
+               static_assert(!FBFP && T >= 32 && C::H == 1, "1-D fp32, at least one warp per transform");
                static_assert(warp_local_exchange<C, C::NP - 2>(), "warp-local last exchange");
+               constexpr int RV = R / 2;      // 16-byte slots per thread row
                const int w = lane >> 5, l = lane & 31;
-               float4* S = reinterpret_cast<float4*>(X + off + 512 * w);
+               float4* S = reinterpret_cast<float4*>(X + off + 32 * R * w);
                const float4* src = reinterpret_cast<const float4*>(static_cast<const float2*>(args.b) +
-                                                                  (size_t)filter_off(args, tr) + 512 * w);
+                                                                  (size_t)filter_off(args, tr) + 32 * R * w);
                __syncwarp();                 // every lane is past its last forward read
 #pragma unroll
-               for(int i = 0; i < 8; ++i) {
+               for(int i = 0; i < RV; ++i) {
                   const float4 v = active ? __ldg(src + l + 32 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
                   S[32 * i + (l ^ (((l >> 3) + 4 * i) & 7))] = v;
                }
                __syncwarp();
 #pragma unroll
-               for(int i = 0; i < 8; ++i) {
-                  const float4 v = S[8 * l + (i ^ (l & 7))];
+               for(int i = 0; i < RV; ++i) {
+                  const int q = RV * l + i;
+                  const float4 v = S[q ^ ((q >> 3) & 7)];
                   f[2 * i] = make_float2(v.x, v.y);
                   f[2 * i + 1] = make_float2(v.z, v.w);
                }
@@ -777,11 +781,20 @@ template<In IN, Out OUT> constexpr int resident_threads()
 #define FUFFT_RESIDENT_THREADS_CONV_DIRECT 768
 #endif
 constexpr int CONV_DIRECT_MIN_N = 2048;
+// fp32 radix-8 convolution of n >= 2048 (one transform per CTA, 256 or 512
+// threads): two or more CTAs per SM at <= 64 registers.  At the 512-thread
+// target one 512-thread CTA of 67 registers filled the SM: 16 warps, issue
+// 44% (ncu, n = 4096).
+#ifndef FUFFT_RESIDENT_THREADS_R8
+#define FUFFT_RESIDENT_THREADS_R8 1024
+#endif
 template<class C, In IN, Out OUT, Flt FLT> constexpr int resident_for()
 {
    return (((IN == In::C32 && OUT == Out::C32) || (IN == In::REAL2 && OUT == Out::REAL2)) &&
            (FLT == Flt::BP_DIRECT || FLT == Flt::LIN_STAGED) && C::H == 1 && C::R == 16 && C::N >= CONV_DIRECT_MIN_N)
              ? FUFFT_RESIDENT_THREADS_CONV_DIRECT
+        : (IN == In::C32 && OUT == Out::C32 && C::H == 1 && C::R == 8 && C::N >= CONV_DIRECT_MIN_N)
+             ? FUFFT_RESIDENT_THREADS_R8
              : resident_threads<IN, OUT>();
 }
 

@@ -262,17 +262,22 @@ fufft_status dispatch_apply(int n, fufft_midop mid, bool bperm, const ConvArgs& 
 // tensor load instead of 128-byte-per-thread global reads).  The pipelined
 // kernel needs 16-byte aligned signal and filter and whole 128-byte rows per
 // transform and per filter stride; otherwise the direct kernel runs.
-// fp32 radix-16 convolution with a chain-order filter staged warp by warp
-// (Flt::LIN_STAGED), 512 <= n <= 8192
-template<In IN, Out OUT, Mid MID>
+// fp32 convolution with a chain-order filter staged warp by warp
+// (Flt::LIN_STAGED): radix 16 for 512 <= n <= 8192, radix 8 for 256 <= n <= 4096
+template<int R, In IN, Out OUT, Mid MID>
 fufft_status launch_lin_staged(int n, const ConvArgs& a, cudaStream_t st, int dev)
 {
    switch(n) {
-   case 512: return launch<512, 16, IN, OUT, MID, Flt::LIN_STAGED, false>(a, st, dev);
-   case 1024: return launch<1024, 16, IN, OUT, MID, Flt::LIN_STAGED, false>(a, st, dev);
-   case 2048: return launch<2048, 16, IN, OUT, MID, Flt::LIN_STAGED, false>(a, st, dev);
-   case 4096: return launch<4096, 16, IN, OUT, MID, Flt::LIN_STAGED, false>(a, st, dev);
-   case 8192: return launch<8192, 16, IN, OUT, MID, Flt::LIN_STAGED, false>(a, st, dev);
+   case 256:
+      if constexpr(R == 8) return launch<256, 8, IN, OUT, MID, Flt::LIN_STAGED, false>(a, st, dev);
+      else return FUFFT_ERR_UNSUPPORTED;
+   case 512: return launch<512, R, IN, OUT, MID, Flt::LIN_STAGED, false>(a, st, dev);
+   case 1024: return launch<1024, R, IN, OUT, MID, Flt::LIN_STAGED, false>(a, st, dev);
+   case 2048: return launch<2048, R, IN, OUT, MID, Flt::LIN_STAGED, false>(a, st, dev);
+   case 4096: return launch<4096, R, IN, OUT, MID, Flt::LIN_STAGED, false>(a, st, dev);
+   case 8192:
+      if constexpr(R == 16) return launch<8192, 16, IN, OUT, MID, Flt::LIN_STAGED, false>(a, st, dev);
+      else return FUFFT_ERR_UNSUPPORTED;
    default: return FUFFT_ERR_UNSUPPORTED;
    }
 }
@@ -283,12 +288,14 @@ fufft_status launch_lin_staged(int n, const ConvArgs& a, cudaStream_t st, int de
 template<int R, bool BFP>
 fufft_status dispatch_conv(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
 {
-   // fp32, radix-16 chain-order filter (the reference's v16 layout), n >= 512:
-   // the direct kernel staging the filter through the exchange buffer
-   if constexpr(!BFP && R == 16 && FUFFT_LIN_STAGED) {
-      if(!bperm && mid != FUFFT_MID_NONE && n >= 512 && n <= 8192 && aligned(a.b, 16) && (a.filter_stride * 8) % 16 == 0)
-         return mid == FUFFT_MID_MULTIPLY ? launch_lin_staged<In::C32, Out::C32, Mid::MUL>(n, a, st, dev)
-                                          : launch_lin_staged<In::C32, Out::C32, Mid::CONJ>(n, a, st, dev);
+   // fp32, chain-order filter (the reference's v16 / ip layouts), at least one
+   // warp per transform: the direct kernel staging the filter through the
+   // exchange buffer
+   if constexpr(!BFP && FUFFT_LIN_STAGED) {
+      if(!bperm && mid != FUFFT_MID_NONE && n >= 32 * R && n <= max_n(R) && aligned(a.b, 16) &&
+         (a.filter_stride * 8) % 16 == 0)
+         return mid == FUFFT_MID_MULTIPLY ? launch_lin_staged<R, In::C32, Out::C32, Mid::MUL>(n, a, st, dev)
+                                          : launch_lin_staged<R, In::C32, Out::C32, Mid::CONJ>(n, a, st, dev);
    }
 #ifndef FUFFT_NO_STREAM
    // fp32 signal with a multiply / conjugate-multiply filter in the linear chain order
