@@ -86,6 +86,118 @@ __global__ void __launch_bounds__(256) outer_pass_kernel(const OuterArgs args)
    }
 }
 
+// powers w[k] = W^{jk} of the group twiddle W^j = exp(-2 pi i j / L), from an
+// exact sincospif argument (2j/L is a dyadic fraction) and the product tree
+template<int R>
+__device__ __forceinline__ void outer_twiddles(long long j, float inv_l, float2 (&w)[R])
+{
+   if(j) {
+      float sn, cs;
+      sincospif(-2.0f * (float)j * inv_l, &sn, &cs);
+      twiddle_powers<R>(make_float2(cs, sn), w);
+   } else {
+#pragma unroll
+      for(int k = 1; k < R; ++k) w[k] = make_float2(1.0f, 0.0f);
+   }
+}
+
+// DIF (S = -1): butterfly then W^{jk}; DIT (S = +1): conj(W^{jk}) then butterfly
+template<int R, int S>
+__device__ __forceinline__ void outer_butterfly(float2 (&u)[R], long long j, float inv_l)
+{
+   float2 w[R];
+   outer_twiddles<R>(j, inv_l, w);
+   if constexpr(S > 0) {
+#pragma unroll
+      for(int k = 1; k < R; ++k) u[k] = cmulc(u[k], w[k]);
+   }
+   dft<R, S>(u);
+   if constexpr(S < 0) {
+#pragma unroll
+      for(int k = 1; k < R; ++k) u[k] = cmul(u[k], w[k]);
+   }
+}
+
+// Two consecutive outer levels in one HBM round trip: level A at stride M
+// (args.M) and level B at stride Mb = M / R.  Positions
+//     b*R*M + j' + k2*Mb + k1*M,   k1, k2 < R,  j' < Mb
+// of one block b and one j' form a closed R x R sub-problem: level A runs
+// over k1 (group j = j' + k2*Mb, twiddle W_{RM}^{j k1}), level B over k2
+// (group j', twiddle W_M^{j' k2}).  A CTA of 256 threads takes J = 256/R
+// consecutive j' (128 or 256 contiguous bytes per row: coalesced), does one
+// level in registers (thread = (k2, j') for A, (k1, j') for B), exchanges
+// through a shared tile [k1][k2][j'] (conflict-free both ways: 32 consecutive
+// slots per warp access) and does the other level.  DIF: A then B; DIT: B
+// then A.  In place is safe: a CTA reads its whole tile before it writes.
+template<int R, int S, OuterMode MODE>
+__global__ void __launch_bounds__(256) outer2_pass_kernel(const OuterArgs args)
+{
+   constexpr int J = 256 / R;
+   __shared__ float2 tile[R * R * J];
+   const long long M = args.M, Mb = M / R;
+   const float inv_a = 1.0f / (float)(R * M), inv_b = 1.0f / (float)M;
+   const long long tiles_per_block = Mb / J;
+   const long long ntiles = args.ngroups / (R * J);      // ngroups = batch * n / R
+   const int q = threadIdx.x / J, jj = threadIdx.x % J;
+   for(long long t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      const long long b = t / tiles_per_block, jp = (t % tiles_per_block) * J + jj;
+      const long long base = b * R * M + jp;
+      float2 u[R];
+      if constexpr(S < 0) {
+         // level A, thread (k2 = q): taps k1 at base + q*Mb + k1*M
+         const long long pa = base + q * Mb;
+         if constexpr(MODE == OuterMode::BFP_IN) {
+            const float sc = __ldg(args.scale + (base >> args.logn));
+            const uint32_t* w = static_cast<const uint32_t*>(args.src);
+#pragma unroll
+            for(int k = 0; k < R; ++k) u[k] = bfp_dequant(ld_stream(w + pa + k * M), sc);
+         } else {
+            const float2* x = static_cast<const float2*>(args.src);
+#pragma unroll
+            for(int k = 0; k < R; ++k) u[k] = ld_stream(x + pa + k * M);
+         }
+         outer_butterfly<R, S>(u, jp + q * Mb, inv_a);
+#pragma unroll
+         for(int k = 0; k < R; ++k) tile[(k * R + q) * J + jj] = u[k];
+         __syncthreads();
+         // level B, thread (k1 = q): taps k2
+#pragma unroll
+         for(int k = 0; k < R; ++k) u[k] = tile[(q * R + k) * J + jj];
+         outer_butterfly<R, S>(u, jp, inv_b);
+         const long long pb = base + q * M;
+#pragma unroll
+         for(int k = 0; k < R; ++k) st_stream(args.dst + pb + k * Mb, u[k]);
+      } else {
+         // level B first, thread (k1 = q): taps k2 at base + q*M + k2*Mb
+         const float2* x = static_cast<const float2*>(args.src);
+         const long long pb = base + q * M;
+#pragma unroll
+         for(int k = 0; k < R; ++k) u[k] = ld_stream(x + pb + k * Mb);
+         outer_butterfly<R, S>(u, jp, inv_b);
+#pragma unroll
+         for(int k = 0; k < R; ++k) tile[(q * R + k) * J + jj] = u[k];
+         __syncthreads();
+         // level A, thread (k2 = q): taps k1
+#pragma unroll
+         for(int k = 0; k < R; ++k) u[k] = tile[(k * R + q) * J + jj];
+         outer_butterfly<R, S>(u, jp + q * Mb, inv_a);
+         const long long pa = base + q * Mb;
+#pragma unroll
+         for(int k = 0; k < R; ++k) st_stream(args.dst + pa + k * M, u[k]);
+         if constexpr(MODE == OuterMode::F32_ABSMAX) {
+            // the whole tile lies in one transform (R*M <= n)
+            float m = 0.0f;
+#pragma unroll
+            for(int k = 0; k < R; ++k) m = fmaxf(m, fmaxf(fabsf(u[k].x), fabsf(u[k].y)));
+#pragma unroll
+            for(int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if((threadIdx.x & 31) == 0) atomicMax(args.absmax + (base >> args.logn), __float_as_uint(m));
+         }
+      }
+      __syncthreads();   // the next tile reuses the shared tile
+   }
+}
+
 namespace host {
 
 template<int R, int S, OuterMode MODE>
@@ -104,6 +216,83 @@ template<int S, OuterMode MODE>
 static fufft_status outer_r(int r, const OuterArgs& a, cudaStream_t st, int device)
 {
    return r == 8 ? outer<8, S, MODE>(a, st, device) : outer<16, S, MODE>(a, st, device);
+}
+
+// levels at strides a.M and a.M / R in one launch (outer2_pass_kernel)
+template<int R, int S, OuterMode MODE>
+static fufft_status outer2(OuterArgs a, cudaStream_t st, int device)
+{
+   a.logM = ilog2c(a.M);
+   a.logn = ilog2c(a.n);
+   const long long tiles = a.ngroups / 256;
+   const long long cap = (long long)sm_count(device) * 8;
+   outer2_pass_kernel<R, S, MODE><<<(unsigned)(tiles < cap ? tiles : cap), 256, 0, st>>>(a);
+   count_launch();
+   return check(cudaGetLastError());
+}
+
+#ifndef FUFFT_OUTER_FUSE
+#define FUFFT_OUTER_FUSE 1
+#endif
+// The outer levels of one direction, fused two by two where possible (a pair
+// needs the inner stride M/R >= 256/R columns).  DIF (S = -1): strides
+// m_top, m_top/R, ..., R*mid... down to mid, pairs from the top; the first
+// launch may dequantise int16 input (first_mode BFP_IN).  DIT (S = +1):
+// strides mid, mid*R, ..., pairs from the bottom; the last launch may reduce
+// the per-transform abs-max (last_mode F32_ABSMAX).
+template<int S>
+static fufft_status outer_levels(int r, OuterArgs a, long long mid, int lout, bool bfp_in, bool absmax,
+                                 float2* ws_after_first, cudaStream_t st, int device)
+{
+   const long long n = a.n;
+   fufft_status s = FUFFT_OK;
+   if constexpr(S < 0) {
+      long long M = n / r;
+      for(int l = 0; l < lout;) {
+         const bool first = l == 0;
+         const bool pair = FUFFT_OUTER_FUSE && l + 1 < lout && M / r >= 256 / r;
+         a.M = (int)M;
+         if(pair) {
+            if(first && bfp_in)
+               s = r == 8 ? outer2<8, -1, OuterMode::BFP_IN>(a, st, device) : outer2<16, -1, OuterMode::BFP_IN>(a, st, device);
+            else
+               s = r == 8 ? outer2<8, -1, OuterMode::F32>(a, st, device) : outer2<16, -1, OuterMode::F32>(a, st, device);
+            M /= (long long)r * r;
+            l += 2;
+         } else {
+            s = (first && bfp_in) ? outer_r<-1, OuterMode::BFP_IN>(r, a, st, device)
+                                  : outer_r<-1, OuterMode::F32>(r, a, st, device);
+            M /= r;
+            l += 1;
+         }
+         if(s != FUFFT_OK) return s;
+         if(first && ws_after_first) a.src = ws_after_first;   // later passes read the fp32 workspace
+      }
+   } else {
+      long long M = mid;
+      for(int l = 0; l < lout;) {
+         const bool pair = FUFFT_OUTER_FUSE && l + 1 < lout && M >= 256 / r;
+         const bool last = l + (pair ? 2 : 1) == lout;
+         if(pair) {
+            a.M = (int)(M * r);
+            if(last && absmax)
+               s = r == 8 ? outer2<8, 1, OuterMode::F32_ABSMAX>(a, st, device)
+                          : outer2<16, 1, OuterMode::F32_ABSMAX>(a, st, device);
+            else
+               s = r == 8 ? outer2<8, 1, OuterMode::F32>(a, st, device) : outer2<16, 1, OuterMode::F32>(a, st, device);
+            M *= (long long)r * r;
+            l += 2;
+         } else {
+            a.M = (int)M;
+            s = (last && absmax) ? outer_r<+1, OuterMode::F32_ABSMAX>(r, a, st, device)
+                                 : outer_r<+1, OuterMode::F32>(r, a, st, device);
+            M *= r;
+            l += 1;
+         }
+         if(s != FUFFT_OK) return s;
+      }
+   }
+   return FUFFT_OK;
 }
 
 }  // namespace host
@@ -215,19 +404,10 @@ fufft_status fufft_conv_large_f32(float* buf, const float* b, int64_t n, int64_t
    oa.src = x;
    oa.n = n;
    oa.ngroups = batch * n / r_out;
-   long long M = n / r_out;
-   for(int l = 0; l < lout; ++l, M /= r_out) {
-      oa.M = (int)M;
-      if((s = outer_r<-1, OuterMode::F32>(r_out, oa, st, c.device)) != FUFFT_OK) return s;
-   }
+   if((s = outer_levels<-1>(r_out, oa, mid, lout, false, false, nullptr, st, c.device)) != FUFFT_OK) return s;
    if((s = run_middle(x, b, nullptr, batch * n / mid, mid, n / mid, layout, midop, false, c, st)) != FUFFT_OK)
       return s;
-   M = mid;
-   for(int l = 0; l < lout; ++l, M *= r_out) {
-      oa.M = (int)M;
-      if((s = outer_r<+1, OuterMode::F32>(r_out, oa, st, c.device)) != FUFFT_OK) return s;
-   }
-   return FUFFT_OK;
+   return outer_levels<+1>(r_out, oa, mid, lout, false, false, nullptr, st, c.device);
 }
 
 size_t fufft_conv_large_bfp_workspace(int64_t n, int64_t batch)
@@ -307,31 +487,18 @@ fufft_status fufft_conv_large_bfp(const int16_t* aq, const float* a_scale, const
    OuterArgs oa{};
    oa.n = n;
    oa.ngroups = batch * n / r_out;
-   // first DIF pass dequantises into the fp32 workspace
-   long long M = n / r_out;
+   // the first DIF launch dequantises into the fp32 workspace
    oa.src = aq;
    oa.dst = ws;
    oa.scale = a_scale;
-   oa.M = (int)M;
-   if((s = outer_r<-1, OuterMode::BFP_IN>(r_out, oa, st, c.device)) != FUFFT_OK) return s;
-   oa.src = ws;
-   for(int l = 1; l < lout; ++l) {
-      M /= r_out;
-      oa.M = (int)M;
-      if((s = outer_r<-1, OuterMode::F32>(r_out, oa, st, c.device)) != FUFFT_OK) return s;
-   }
+   if((s = outer_levels<-1>(r_out, oa, mid, lout, true, false, ws, st, c.device)) != FUFFT_OK) return s;
    if((s = run_middle(ws, bq, b_scale, batch * n / mid, mid, n / mid, layout, midop, true, c, st)) != FUFFT_OK)
       return s;
-   // inverse passes; the last one also reduces the per-transform abs-max into o_scale
+   // inverse passes; the last launch also reduces the per-transform abs-max into o_scale
    if((s = check(cudaMemsetAsync(o_scale, 0, sizeof(float) * batch, st))) != FUFFT_OK) return s;
-   M = mid;
-   for(int l = 0; l < lout; ++l, M *= r_out) {
-      oa.M = (int)M;
-      oa.absmax = reinterpret_cast<unsigned int*>(o_scale);
-      s = (l == lout - 1) ? outer_r<+1, OuterMode::F32_ABSMAX>(r_out, oa, st, c.device)
-                          : outer_r<+1, OuterMode::F32>(r_out, oa, st, c.device);
-      if(s != FUFFT_OK) return s;
-   }
+   oa.src = ws;
+   oa.absmax = reinterpret_cast<unsigned int*>(o_scale);
+   if((s = outer_levels<+1>(r_out, oa, mid, lout, false, true, nullptr, st, c.device)) != FUFFT_OK) return s;
    return bfp_requantize(ws, o_scale, reinterpret_cast<uint32_t*>(oq), n, batch, st);
 }
 

@@ -150,3 +150,38 @@ def test_large_full_size_properties(ops):
     assert float((rt / n - a).abs().pow(2).sum() / a.abs().pow(2).sum()) ** 0.5 < 2e-6
     torch.cuda.synchronize()
     assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("n,r_out,mid,lname", [(262144, 16, 1024, "R16"), (262144, 8, 4096, "R8"),
+                                               (1 << 21, 16, 512, "R16_BPERM"), (1 << 21, 8, 4096, "R8")])
+def test_large_multi_level_plans(ops, oracle, n, r_out, mid, lname):
+    """two and three outer levels (radix 16 and 8): pairs of levels run as one
+    fused pass, an odd level alone; fp32 and int16-BFP against the oracle's
+    four-step on the same chain"""
+    layout = getattr(ops, "LAYOUT_" + lname)
+    mr = 16 if lname.startswith("R16") else 8
+    batch = 2 if n <= 262144 else 1
+    rng = np.random.default_rng(n + r_out)
+    a = (rng.standard_normal(n * batch) + 1j * rng.standard_normal(n * batch)).astype(np.complex64)
+    taps = rng.uniform(-1, 1, n * batch) + 1j * rng.uniform(-1, 1, n * batch)
+    spec = (np.fft.fft(taps.reshape(batch, n), axis=1) / n).astype(np.complex64)
+    rev = oracle.rev_table(oracle.foursteps_chain(n, r_out, mid, mr), n)
+    b_dr = np.ascontiguousarray(spec[:, rev]).ravel()
+    bk = _chunk_bperm(b_dr, mid, mr) if lname.endswith("BPERM") else b_dr
+    want = oracle.conv_foursteps(a, b_dr, n, r_out, mid, mr)
+    got = ops.conv_large(_dev(a), _dev(bk), n, layout, r_out=r_out, mid_size=mid).cpu().numpy()
+    assert rel_l2(got, want) <= F32_TOL
+    assert rel_l2(got[:n], oracle.conv_f64(a[:n], spec[0], n)) < 5e-6
+    # int16-BFP on the same plan
+    aq, as_ = oracle.bfp_quantize(a, n)
+    bq, bs = oracle.bfp_quantize(b_dr, n)
+    bqk = bq if not lname.endswith("BPERM") else \
+        _chunk_bperm(bq.view(np.int32).ravel(), mid, mr).view(np.int16).reshape(-1, 2)
+    want_f = oracle.conv_foursteps(oracle.bfp_dequantize(aq, as_, n), oracle.bfp_dequantize(bq, bs, n),
+                                   n, r_out, mid, mr)
+    wq, ws = oracle.bfp_quantize(want_f, n)
+    oq, os_ = ops.conv_large_bfp(_dev(aq), _dev(as_), _dev(bqk), _dev(bs), n, layout, r_out=r_out, mid_size=mid)
+    got = oracle.bfp_dequantize(oq.cpu().numpy(), os_.cpu().numpy(), n)
+    assert rel_l2(got, oracle.bfp_dequantize(wq, ws, n)) <= BFP_TOL
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
