@@ -661,6 +661,40 @@ def run_ncu_all():
         print(json.dumps({"call": label, "launches": launches, "points": points, "algorithmic_bytes": nbytes}))
 
 
+def run_ncu_dist():
+    """one process, two GPUs: one fused exchange launch of each kind per GPU
+    (fufft_dist_pass_push: first DIF pass + NVLink stores into the peer's
+    block; fufft_dist_pass_pull: NVLink loads + last DIT pass), n = 2^24, for
+    an ncu capture of NVLink and DRAM bytes"""
+    import ctypes as ct
+    import torch
+    from fufft_b200 import multi_gpu as mg
+    from fufft_b200 import ops
+    from fufft_b200._lib import check, lib
+    world, n = 2, 1 << 24
+    for d in range(world):
+        torch.cuda.set_device(d)
+        ops.init()
+    cols = n // (world * world)
+    slices, bb = [], []
+    for r in range(world):
+        g = torch.Generator(device=f"cuda:{r}")
+        g.manual_seed(r)
+        slices.append(torch.randn(world * cols, dtype=torch.complex64, device=f"cuda:{r}", generator=g))
+        bb.append(torch.randn(n // world, dtype=torch.complex64, device=f"cuda:{r}", generator=g) / n)
+    blocks = mg.conv_single_signal(slices, bb, n)       # enables peer access, allocates the blocks
+    for r in range(world):
+        torch.cuda.synchronize(r)
+    addrs = (ct.c_uint64 * world)(*[b.data_ptr() for b in blocks])
+    L = lib()
+    for fn, name in ((L.fufft_dist_pass_push, "push"), (L.fufft_dist_pass_pull, "pull")):
+        for r in range(world):
+            with torch.cuda.device(r):
+                check(fn(torch.view_as_real(slices[r]).data_ptr(), addrs, world, r, cols, n,
+                         torch.cuda.current_stream().cuda_stream), name)
+                torch.cuda.synchronize(r)
+
+
 def run_ncu_case(which: str = "headline"):
     """one launch of each kernel of a group, on a batch of a few hundred MB
     (> L2), for ncu.  headline: fp32 (register-boundary filter), fp32 (linear
@@ -956,8 +990,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-configs", action="store_true", help="headline only (no per-config records)")
     ap.add_argument("--no-dist", action="store_true", help="under torchrun: no single-signal record")
-    ap.add_argument("--ncu-case", nargs="?", const="headline", default=None, choices=["headline", "cluster", "all"],
-                    help="one launch per kernel of a group, for ncu")
+    ap.add_argument("--ncu-case", nargs="?", const="headline", default=None,
+                    choices=["headline", "cluster", "all", "dist"],
+                    help="one launch per kernel of a group, for ncu (dist: two GPUs, one process)")
     ap.add_argument("--dist-mode", choices=["p2p", "nccl"], default="p2p",
                     help="dist: all-to-alls fused into the outer passes over NVLink (p2p) or NCCL all_to_all")
     ap.add_argument("--configs", default="1,2,3,4,5,6,7",
@@ -969,6 +1004,9 @@ def main():
     args = ap.parse_args()
     if args.ncu_case == "all":
         run_ncu_all()
+        return
+    if args.ncu_case == "dist":
+        run_ncu_dist()
         return
     if args.ncu_case:
         run_ncu_case(args.ncu_case)
