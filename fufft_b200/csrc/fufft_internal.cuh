@@ -308,8 +308,10 @@ fufft_status dispatch_conv(int n, fufft_midop mid, bool bperm, const ConvArgs& a
       }
    }
 #endif
-   return BFP ? dispatch_mid<R, In::BFP, Out::BFP, true>(n, mid, bperm, a, st, dev)
-              : dispatch_mid<R, In::C32, Out::C32, false>(n, mid, bperm, a, st, dev);
+   // if constexpr: each kernel family's translation unit instantiates only its
+   // own kernels (one definition of every kernel in the library)
+   if constexpr(BFP) return dispatch_mid<R, In::BFP, Out::BFP, true>(n, mid, bperm, a, st, dev);
+   else return dispatch_mid<R, In::C32, Out::C32, false>(n, mid, bperm, a, st, dev);
 }
 
 // one entry per kernel family and radix (each lives in its own translation
