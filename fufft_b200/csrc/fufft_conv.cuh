@@ -791,7 +791,7 @@ constexpr int CONV_DIRECT_MIN_N = 2048;
 template<class C, In IN, Out OUT, Flt FLT> constexpr int resident_for()
 {
    return (((IN == In::C32 && OUT == Out::C32) || (IN == In::REAL2 && OUT == Out::REAL2)) &&
-           (FLT == Flt::BP_DIRECT || FLT == Flt::LIN_STAGED) && C::H == 1 && C::R == 16 && C::N >= CONV_DIRECT_MIN_N)
+           (FLT == Flt::BP_DIRECT || FLT == Flt::LIN_STAGED) && C::R == 16 && C::N >= CONV_DIRECT_MIN_N)
              ? FUFFT_RESIDENT_THREADS_CONV_DIRECT
         : (IN == In::C32 && OUT == Out::C32 && C::H == 1 && C::R == 8 && C::N >= CONV_DIRECT_MIN_N)
              ? FUFFT_RESIDENT_THREADS_R8

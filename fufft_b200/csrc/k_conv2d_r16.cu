@@ -40,8 +40,32 @@ static fufft_status conv2d_shape(int h, int w, const ConvArgs& a, cudaStream_t s
    return FUFFT_ERR_INVALID_SIZE;
 }
 
+// 4096-point images with rows of 64 or more: the register-boundary filter read
+// straight from global memory at the boundary (coalesced; no shared-memory
+// filter tile, so three CTAs per SM fit), as the 1-D radix-16 kernels do.
+// Measured on B200 (1 GiB batches, A/B against the TMA-staged tile): 64x64
+// +6%, 32x128 +7%, 16x256 +7% (per-image filters) / +22% (one shared
+// filter); 128x32, 2048-point (spills) and 8192-point shapes were 2-24% slower
+// and keep the tile.
+#ifndef FUFFT_2D_FILTER_DIRECT
+#define FUFFT_2D_FILTER_DIRECT 1
+#endif
+template<Mid MID>
+static fufft_status conv2d_direct(int h, int w, const ConvArgs& a, cudaStream_t st, int dev)
+{
+   if(h == 64 && w == 64) return launch_chain<Chain2<64, 64, 16>, In::C32, Out::C32, MID, Flt::BP_DIRECT, false>(a, st, dev);
+   if(h == 32 && w == 128) return launch_chain<Chain2<32, 128, 16>, In::C32, Out::C32, MID, Flt::BP_DIRECT, false>(a, st, dev);
+   if(h == 16 && w == 256) return launch_chain<Chain2<16, 256, 16>, In::C32, Out::C32, MID, Flt::BP_DIRECT, false>(a, st, dev);
+   return FUFFT_ERR_UNSUPPORTED;
+}
+
 fufft_status family_conv2d_r16(int h, int w, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
 {
+   if(FUFFT_2D_FILTER_DIRECT && bperm && mid != FUFFT_MID_NONE) {
+      const fufft_status s = mid == FUFFT_MID_MULTIPLY ? conv2d_direct<Mid::MUL>(h, w, a, st, dev)
+                                                       : conv2d_direct<Mid::CONJ>(h, w, a, st, dev);
+      if(s != FUFFT_ERR_UNSUPPORTED) return s;
+   }
    switch(mid) {
    case FUFFT_MID_NONE: return conv2d_shape<Mid::NONE, Flt::NONE>(h, w, a, st, dev);
    case FUFFT_MID_MULTIPLY:
