@@ -64,30 +64,63 @@ def profile_traffic(key):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled while the timed loop runs"""
-    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle reasons, sampled through NVML (read-only queries)
+    every 2 ms while the timed loop runs; falls back to `nvidia-smi -lms`
+    when NVML is unavailable"""
+    # NVML clocks-event-reason bits
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
 
     def __init__(self, index: int):
-        self.index, self.rows, self.proc = index, [], None
+        self.index, self.rows, self.proc, self.stop = index, [], None, None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "50"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv, self.h = pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+            self.stop = threading.Event()
+            self.t = threading.Thread(target=self._poll, daemon=True)
             self.t.start()
         except Exception:
-            self.proc = None
+            self.nv = None
+            try:
+                self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index),
+                                              "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
+                                              "--format=csv,noheader,nounits", "-lms", "50"],
+                                             stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self.t = threading.Thread(target=self._read, daemon=True)
+                self.t.start()
+            except Exception:
+                self.proc = None
         return self
+
+    def _poll(self):
+        nv = self.nv
+        while not self.stop.is_set():
+            try:
+                mhz = float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                try:
+                    bits = int(nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+                except AttributeError:
+                    bits = int(nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h))
+                self.rows.append((mhz, self.max_mhz, bits))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def _read(self):
         for line in self.proc.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
+            f = [x.strip() for x in line.split(",")]
+            try:
+                self.rows.append((float(f[0]), float(f[1]), int(f[2], 16)))
+            except (ValueError, IndexError):
+                pass
 
     def __exit__(self, *exc):
+        if self.stop is not None:
+            self.stop.set()
+            self.t.join(timeout=2)
         if self.proc:
             self.proc.terminate()
             try:
@@ -97,13 +130,11 @@ class ClockSampler:
             self.t.join(timeout=2)
 
     def summary(self):
-        sm = [float(r[0]) for r in self.rows if len(r) >= 7 and r[0].replace(".", "").isdigit()]
-        if not sm:
+        if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows if len(r) >= 7 for i in range(4) if r[3 + i] == "Active"})
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(float(r[1]) for r in self.rows if len(r) >= 7),
-                "reasons": reasons, "samples": len(sm)}
+        reasons = sorted({name for _, _, bits in self.rows for bit, name in self.REASONS.items() if bits & bit})
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": max(r[1] for r in self.rows),
+                "reasons": reasons, "samples": len(self.rows), "source": "nvml" if self.nv else "nvidia-smi"}
 
 
 # ------------------------------------------------------------------------------------------
@@ -589,8 +620,11 @@ def run_ncu_all():
         man.append((label, launches, points, nbytes))
 
     call("conv fp32 R16_BPERM (register-boundary filter, read directly)", lambda: ops.conv(a, b, n, ops.LAYOUT_R16_BPERM, out=o), pts, 24 * pts)
-    call("conv fp32 R16 (linear filter: pipelined kernel)", lambda: ops.conv(a, b, n, ops.LAYOUT_R16, out=o), pts, 24 * pts)
+    call("conv fp32 R16 (linear mixedrev16 filter, staged per warp)", lambda: ops.conv(a, b, n, ops.LAYOUT_R16, out=o),
+         pts, 24 * pts)
     call("conv fp32 R8_BPERM", lambda: ops.conv(a, b, n, ops.LAYOUT_R8_BPERM, out=o), pts, 24 * pts)
+    call("conv fp32 R8 (linear mixedrev filter, staged per warp)", lambda: ops.conv(a, b, n, ops.LAYOUT_R8, out=o),
+         pts, 24 * pts)
     call("conv fp32 R16_BPERM conj-multiply", lambda: ops.conv(a, b, n, ops.LAYOUT_R16_BPERM, ops.MID_CONJ_MULTIPLY, out=o), pts, 24 * pts)
     aq, as_ = ops.bfp_pack(a, n)
     torch.cuda.synchronize()
@@ -622,8 +656,8 @@ def run_ncu_all():
     call("filter_from_taps R16_BPERM", lambda: ops.filter_from_taps(a, n, ops.LAYOUT_R16_BPERM), pts, 16 * pts)
     call("filter_permute (device)", lambda: ops.filter_permute(a, n, ops.LAYOUT_R16_BPERM), pts, 16 * pts)
     h = w = 64
-    call("conv2d 64x64 one CTA (shared filter)", lambda: ops.conv2d(a, b[: h * w], h, w, ops.LAYOUT_R16_BPERM, filter_stride=0, out=o),
-         pts, 16 * pts)
+    call("conv2d 64x64 one CTA (shared filter, read directly)",
+         lambda: ops.conv2d(a, b[: h * w], h, w, ops.LAYOUT_R16_BPERM, filter_stride=0, out=o), pts, 16 * pts)
     call("conv2d 256x256 cluster (shared filter)", lambda: ops.conv2d(a, b[: 65536], 256, 256, ops.LAYOUT_R16_BPERM, filter_stride=0, out=o),
          pts, 16 * pts)
     n2 = 32768
@@ -646,9 +680,9 @@ def run_ncu_all():
     while q > 1:
         q //= r_out
         lout += 1
-    call(f"four-step N=2^20 multi-kernel ({lout} outer r{r_out} passes each way + middle {mid})",
+    call(f"four-step N=2^20 multi-kernel ({lout} outer r{r_out} levels each way, two per launch, + middle {mid})",
          lambda: ops.conv_large(buf, b, n3, ops.LAYOUT_R16, r_out=r_out, mid_size=mid), pts, 24 * pts,
-         launches=2 * lout + 1)
+         launches=2 * ((lout + 1) // 2) + 1)
     x = a[: 8 * (n3 // 64)].contiguous()
     torch.cuda.synchronize()
     man.append(("(torch copy)", 1, 0, 0))
@@ -698,7 +732,7 @@ def run_ncu_dist():
 def run_ncu_case(which: str = "headline"):
     """one launch of each kernel of a group, on a batch of a few hundred MB
     (> L2), for ncu.  headline: fp32 (register-boundary filter), fp32 (linear
-    chain filter), int16-BFP (linear chain filter) at N=4096; cluster: the
+    chain filter, staged per warp), int16-BFP (linear chain filter) at N=4096; cluster: the
     cluster-fused N=32768 (radix-16 chain and the four-step recipe), 2-D
     256x256 and the int16-BFP four-step N=32768"""
     import torch
