@@ -208,6 +208,39 @@ namespace host {
 #ifndef FUFFT_R2_FILTER_DIRECT
 #define FUFFT_R2_FILTER_DIRECT 1   // two-for-one real: +6-8% at n = 4096, +1% at 2048
 #endif
+// fp32 radix-8 register-boundary layout (R8_BPERM): the filter read straight
+// from global memory for n = 2^k with bit k of the mask set, else the
+// TMA-staged tile.  Measured on B200 (complex convolution, 1 GiB signals,
+// median of three interleaved runs on each of two boxes, % of measured HBM,
+// direct / tile): 512: 104.5 / 88.1 and 97.4 / 86.6; 1024: 74.5 / 64.1 and
+// 69.2 / 64.6; 2048: 76.3 / 74.5 and 73.6 / 76.3 (even, kept on the tile);
+// 4096: 65.4 / 71.0.  (Two radix-8 butterfly groups per thread on 16
+// registers -- half the threads per transform -- measured 66-100% at the
+// same sizes: no gain, not built.)
+#ifndef FUFFT_R8_BP_DIRECT
+#define FUFFT_R8_BP_DIRECT ((1 << 9) | (1 << 10))
+#endif
+constexpr bool in_mask(long long mask, int n)
+{
+   return n > 0 && (1 << ilog2c(n)) == n && ((mask >> ilog2c(n)) & 1);
+}
+// launch_n restricted to the sizes of a mask (instantiates only those)
+template<long long MASK, int R, In IN, Out OUT, Mid MID, Flt FLT, bool FBFP>
+fufft_status launch_masked(int n, const ConvArgs& args, cudaStream_t st, int device)
+{
+#define FUFFT_MCASE(NN)                                                                \
+   case NN:                                                                            \
+      if constexpr(in_mask(MASK, NN) && NN >= R && NN <= (R == 8 ? MAX_N_R8 : MAX_N_R16)) \
+         return launch<NN, R, IN, OUT, MID, FLT, FBFP>(args, st, device);              \
+      else return FUFFT_ERR_UNSUPPORTED;
+   switch(n) {
+      FUFFT_MCASE(8) FUFFT_MCASE(16) FUFFT_MCASE(32) FUFFT_MCASE(64) FUFFT_MCASE(128) FUFFT_MCASE(256)
+      FUFFT_MCASE(512) FUFFT_MCASE(1024) FUFFT_MCASE(2048) FUFFT_MCASE(4096) FUFFT_MCASE(8192)
+   default: return FUFFT_ERR_UNSUPPORTED;
+   }
+#undef FUFFT_MCASE
+}
+
 template<int R, In IN, Out OUT, bool FBFP>
 fufft_status dispatch_mid(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
 {
@@ -216,6 +249,12 @@ fufft_status dispatch_mid(int n, fufft_midop mid, bool bperm, const ConvArgs& a,
       if(bperm && n >= CONV_DIRECT_MIN_N && mid != FUFFT_MID_NONE)
          return mid == FUFFT_MID_MULTIPLY ? launch_n<R, IN, OUT, Mid::MUL, Flt::BP_DIRECT, FBFP>(n, a, st, dev)
                                           : launch_n<R, IN, OUT, Mid::CONJ, Flt::BP_DIRECT, FBFP>(n, a, st, dev);
+   }
+   if constexpr(R == 8 && !FBFP && IN == In::C32 && OUT == Out::C32) {
+      constexpr long long M = FUFFT_R8_BP_DIRECT;
+      if(bperm && mid != FUFFT_MID_NONE && in_mask(M, n) && n <= MAX_N_R8)
+         return mid == FUFFT_MID_MULTIPLY ? launch_masked<M, R, IN, OUT, Mid::MUL, Flt::BP_DIRECT, FBFP>(n, a, st, dev)
+                                          : launch_masked<M, R, IN, OUT, Mid::CONJ, Flt::BP_DIRECT, FBFP>(n, a, st, dev);
    }
    switch(mid) {
    case FUFFT_MID_NONE: return launch_n<R, IN, OUT, Mid::NONE, Flt::NONE, FBFP>(n, a, st, dev);

@@ -102,6 +102,24 @@ def test_conv_broadcast_filter_and_inplace(ops, oracle):
     assert out.data_ptr() == da.data_ptr()
 
 
+@pytest.mark.parametrize("n", [512, 1024, 2048, 4096])
+@pytest.mark.parametrize("lname", ["R8", "R8_BPERM"])
+def test_conv_r8_filter_paths(ops, oracle, n, lname):
+    """radix-8 layouts: the register-boundary filter read from global memory
+    (R8_BPERM, 512 and 1024), the TMA-staged tile (R8_BPERM, 2048 and 4096) and the
+    chain-order filter staged per warp (R8): shared and per-transform filters,
+    both mid-ops, an odd batch (a partly filled CTA below 2048)"""
+    layout, radix, v = LAYOUTS[lname]
+    batch = 7
+    a, b = oracle.gen_test(n, 1, batch)
+    for mid in (MID_MULTIPLY, MID_CONJ):
+        for fs in (n, 0):
+            bb = b if fs else b[:n]
+            want = oracle.conv(a, oracle.permute_dr(bb, n, radix), n, radix, mid, filter_stride=fs)
+            got = _host(ops.conv(_dev(a), _dev(_filter(oracle, bb, n, radix, v)), n, layout, mid, filter_stride=fs))
+            assert rel_l2(got, want) <= F32_TOL, (mid, fs)
+
+
 def test_device_filter_permute_bit_exact(ops, oracle):
     rng = np.random.default_rng(1)
     for n in (64, 512, 2048, 4096, 8192):      # shared-memory staged gather (8192: 64 KB)
