@@ -409,15 +409,34 @@ def run_configs(args, ops, torch, dist, hbm, rank, world, dev):
                 "frac": round(gbs / hbm, 4), "bytes_per_point": bpp, **kw}
 
     res = {}
-    # config 1: N=1024 x 4096 (32 MiB per array: inside L2, so L2 is flushed before every step)
-    n, batch = 1024, 4096
-    a, spec, bperm = make_inputs(ops, torch, n, batch, 1000 * 1 + n + rank, dev)
-    o = torch.empty_like(a)
-    ms = time_flushed(torch, lambda: ops.conv(a, bperm, n, ops.LAYOUT_R16_BPERM, out=o), steps, warm, dist=dist)
-    res["c1_fp32_n1024_b4096"] = rec(ms, batch * n, 24, layout="R16_BPERM", l2="flushed before every step",
+    # config 1: N=1024 x 4096 (32 MiB per array: inside L2).  Throughput of
+    # back-to-back batches: four independent input/output sets (384 MiB in all,
+    # > 3x L2) in turn, so every step's inputs were evicted by the three steps
+    # before it.  Also the latency of one isolated launch with L2 flushed
+    # before it (event-timed, so it carries the ~6 us launch-and-event floor of
+    # any kernel timed alone: an empty kernel times at 6 us the same way)
+    n, batch, nsets = 1024, 4096, 4
+    sets = []
+    for k in range(nsets):
+        a, spec, bperm = make_inputs(ops, torch, n, batch, 1000 * 1 + 10 * k + n + rank, dev)
+        del spec
+        sets.append((a, bperm, torch.empty_like(a)))
+    turn = [0]
+
+    def c1_step():
+        a, bperm, o = sets[turn[0] % nsets]
+        turn[0] += 1
+        ops.conv(a, bperm, n, ops.LAYOUT_R16_BPERM, out=o)
+    ms = time_steps(torch, c1_step, steps * nsets, warm, dist)
+    a, bperm, o = sets[0]
+    ms1 = time_flushed(torch, lambda: ops.conv(a, bperm, n, ops.LAYOUT_R16_BPERM, out=o), steps, warm, dist=dist)
+    res["c1_fp32_n1024_b4096"] = rec(ms, batch * n, 24, layout="R16_BPERM",
+                                     l2=f"{nsets} input/output sets in turn ({nsets * 96} MiB > 3x L2)",
+                                     single_launch_ms=round(ms1, 4),
+                                     single_launch_l2="flushed before the launch",
                                      parity=parity_f32_1d(ops, torch, a, lambda ii: unbperm_rows(bperm.view(batch, n)[ii], n),
                                                           o, n, batch, sample_idx(batch, 1)))
-    del a, spec, bperm, o
+    del sets, a, bperm, o
 
     # config 2: the other sizes of the sweep (1 GiB of signal), fp32 and int16-BFP;
     # at N=4096 also the reference's own linear filter orders (radix-16 and radix-8 chains)
@@ -859,8 +878,18 @@ def run_sweep(args):
         o = torch.empty_like(a)
         for lay, name in [(ops.LAYOUT_R16_BPERM, "R16_BPERM"), (ops.LAYOUT_R16, "R16")]:
             ms = time_flushed(torch, lambda: ops.conv(a, b, n, lay, out=o), steps, warm)
-            emit(f"1: fp32 N={n} batch={batch} {name} (L2 flushed per step)", ms, batch * n, 24)
-        del a, b, o
+            emit(f"1: fp32 N={n} batch={batch} {name} (one launch, L2 flushed before it)", ms, batch * n, 24)
+        # back-to-back batches over four input/output sets (384 MiB > 3x L2)
+        sets = [(torch.randn_like(a), torch.randn_like(b), torch.empty_like(o)) for _ in range(4)]
+        turn = [0]
+
+        def step():
+            x, f, y = sets[turn[0] % 4]
+            turn[0] += 1
+            ops.conv(x, f, n, ops.LAYOUT_R16_BPERM, out=y)
+        ms = time_steps(torch, step, 4 * steps, warm, None)
+        emit(f"1: fp32 N={n} batch={batch} R16_BPERM (back-to-back, 4 sets in turn)", ms, batch * n, 24)
+        del a, b, o, sets
     # config 2: size sweep, 1 GiB of signal, fp32 and int16-BFP
     if 2 in cfgs:
         for n in (512, 1024, 2048, 4096):

@@ -92,14 +92,29 @@ fufft_status launch_chain(const ConvArgs& args, cudaStream_t st, int device)
    // over 1 GiB (B200, A/B), neutral for int16-BFP, and -7% for a launch of
    // 3-4 waves (N=1024 x 4096), so fp32 launches of 8 waves or more only
    const long long res = resident[device & 63].load();
+   ConvArgs a2 = args;
    if(FUFFT_L2_PREFETCH && IN == In::C32 && aligned(args.a, 16) && (MID == Mid::NONE || aligned(args.b, 16)) &&
-      res > 0 && grid >= 8 * res) {
-      ConvArgs a2 = args;
+      res > 0 && grid >= 8 * res)
       a2.prefetch_ahead = res;
-      kern<<<(unsigned)grid, K::THREADS, K::SMEM, st>>>(a2);
-   } else {
-      kern<<<(unsigned)grid, K::THREADS, K::SMEM, st>>>(args);
-   }
+#if FUFFT_PDL
+   // programmatic dependent launch: this grid may be scheduled while the
+   // stream's previous kernel finishes (its CTAs wait on griddepcontrol.wait
+   // before touching global memory, so every dependency still holds)
+   cudaLaunchConfig_t cfg = {};
+   cfg.gridDim = dim3((unsigned)grid);
+   cfg.blockDim = dim3(K::THREADS);
+   cfg.dynamicSmemBytes = K::SMEM;
+   cfg.stream = st;
+   cudaLaunchAttribute at[1];
+   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+   at[0].val.programmaticStreamSerializationAllowed = 1;
+   cfg.attrs = at;
+   cfg.numAttrs = 1;
+   fufft_status ls = check(cudaLaunchKernelEx(&cfg, kern, a2));
+   if(ls != FUFFT_OK) return ls;
+#else
+   kern<<<(unsigned)grid, K::THREADS, K::SMEM, st>>>(a2);
+#endif
    count_launch();
    return check(cudaGetLastError());
 }
