@@ -63,78 +63,114 @@ def profile_traffic(key):
         return None
 
 
+_SAMPLER = r"""
+import sys, time
+import pynvml as nv
+nv.nvmlInit()
+key = sys.argv[1]
+h = nv.nvmlDeviceGetHandleByPciBusId(key) if ":" in key else nv.nvmlDeviceGetHandleByIndex(int(key))
+mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+rf = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or nv.nvmlDeviceGetCurrentClocksThrottleReasons
+print("ready", flush=True)
+while True:
+    t = time.monotonic()
+    print(t, nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), mx, int(rf(h)), flush=True)
+    time.sleep(0.001)
+"""
+
+
 class ClockSampler:
-    """SM clock and throttle reasons, sampled through NVML (read-only queries)
-    every 2 ms while the timed loop runs; falls back to `nvidia-smi -lms`
-    when NVML is unavailable"""
+    """SM clock and throttle reasons of one GPU, sampled through NVML
+    (read-only queries) every millisecond by a separate process, so that the
+    samples do not wait for this process's interpreter lock.  Each sample
+    carries a CLOCK_MONOTONIC time stamp; `mark()` / `mark(end=True)` bound the
+    timed region and the summary keeps the samples inside it.  Falls back to
+    `nvidia-smi -lms` when NVML is unavailable."""
     # NVML clocks-event-reason bits
     REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
 
-    def __init__(self, index: int):
-        self.index, self.rows, self.proc, self.stop = index, [], None, None
+    def __init__(self, device: int):
+        self.device, self.rows, self.proc, self.t, self.source = device, [], None, None, None
+        self.t0, self.t1 = None, None
+
+    def _key(self):
+        try:
+            import torch
+            p = torch.cuda.get_device_properties(self.device)
+            return "%08x:%02x:%02x.0" % (p.pci_domain_id, p.pci_bus_id, p.pci_device_id)
+        except Exception:
+            return str(self.device)
 
     def __enter__(self):
         try:
-            import pynvml
-            pynvml.nvmlInit()
-            self.nv, self.h = pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
-            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
-            self.stop = threading.Event()
-            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER, self._key()], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            if self.proc.stdout.readline().strip() != "ready":
+                raise RuntimeError("sampler did not start")
+            self.source = "nvml"
+            self.t = threading.Thread(target=self._read, args=(False,), daemon=True)
             self.t.start()
         except Exception:
-            self.nv = None
+            self._stop()
             try:
-                self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index),
+                self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device),
                                               "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
-                                              "--format=csv,noheader,nounits", "-lms", "50"],
+                                              "--format=csv,noheader,nounits", "-lms", "20"],
                                              stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-                self.t = threading.Thread(target=self._read, daemon=True)
+                self.source = "nvidia-smi"
+                self.t = threading.Thread(target=self._read, args=(True,), daemon=True)
                 self.t.start()
             except Exception:
                 self.proc = None
         return self
 
-    def _poll(self):
-        nv = self.nv
-        while not self.stop.is_set():
-            try:
-                mhz = float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
-                try:
-                    bits = int(nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
-                except AttributeError:
-                    bits = int(nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h))
-                self.rows.append((mhz, self.max_mhz, bits))
-            except Exception:
-                pass
-            time.sleep(0.002)
-
-    def _read(self):
+    def _read(self, smi):
         for line in self.proc.stdout:
-            f = [x.strip() for x in line.split(",")]
             try:
-                self.rows.append((float(f[0]), float(f[1]), int(f[2], 16)))
+                if smi:
+                    f = [x.strip() for x in line.split(",")]
+                    self.rows.append((time.monotonic(), float(f[0]), float(f[1]), int(f[2], 16)))
+                else:
+                    f = line.split()
+                    self.rows.append((float(f[0]), float(f[1]), float(f[2]), int(f[3])))
             except (ValueError, IndexError):
                 pass
 
-    def __exit__(self, *exc):
-        if self.stop is not None:
-            self.stop.set()
-            self.t.join(timeout=2)
+    def mark(self, end=False):
+        if end:
+            self.t1 = time.monotonic()
+        else:
+            self.t0 = time.monotonic()
+
+    def _stop(self):
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
+        if self.t:
             self.t.join(timeout=2)
 
+    def __exit__(self, *exc):
+        self._stop()
+
     def summary(self):
-        if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        reasons = sorted({name for _, _, bits in self.rows for bit, name in self.REASONS.items() if bits & bit})
-        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": max(r[1] for r in self.rows),
-                "reasons": reasons, "samples": len(self.rows), "source": "nvml" if self.nv else "nvidia-smi"}
+        rows = self.rows
+        if self.t0 is not None and self.t1 is not None:
+            inside = [r for r in rows if self.t0 <= r[0] <= self.t1]
+            window = "timed region"
+            if not inside:   # region shorter than one sample interval: the samples around it
+                inside = [r for r in rows if self.t0 - 0.01 <= r[0] <= self.t1 + 0.01]
+                window = "timed region +- 10 ms"
+            rows = inside
+        else:
+            window = "whole block"
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "window": window}
+        reasons = sorted({name for *_, bits in rows for bit, name in self.REASONS.items() if bits & bit})
+        return {"sm_mhz": statistics.median(r[1] for r in rows), "sm_max_mhz": max(r[2] for r in rows),
+                "reasons": reasons, "samples": len(rows), "source": self.source, "window": window}
 
 
 # ------------------------------------------------------------------------------------------
@@ -267,7 +303,7 @@ def parity_bfp_1d(ops, torch, aq, as_, bq, bs, oq, os_, n, batch, idx, radices=N
             "checked": len(idx)}
 
 
-def time_steps(torch, fn, steps, warmup, dist):
+def time_steps(torch, fn, steps, warmup, dist, clk=None):
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -275,11 +311,15 @@ def time_steps(torch, fn, steps, warmup, dist):
         dist.barrier()
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if clk:
+        clk.mark()
     e0.record(st)
     for _ in range(steps):
         fn()
     e1.record(st)
     torch.cuda.synchronize()
+    if clk:
+        clk.mark(end=True)
     if dist:
         dist.barrier()
     ms = e0.elapsed_time(e1) / steps
@@ -316,7 +356,7 @@ def run_ours(args, rank, world, dist):
     launches0 = ops.launch_count()
     with ClockSampler(torch.cuda.current_device()) as clk:
         ms = time_steps(torch, lambda: ops.conv(a, bperm, n, layout, ops.MID_MULTIPLY, out=out),
-                        args.steps, args.warmup, dist)
+                        args.steps, args.warmup, dist, clk)
     launches = (ops.launch_count() - launches0) // (args.steps + args.warmup) * args.steps
     pts = batch * n
     gpts = pts / (ms * 1e-3) / 1e9
