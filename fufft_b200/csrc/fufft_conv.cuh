@@ -41,8 +41,10 @@ enum class Mid { NONE, MUL, CONJ };        // pointwise operation between the tr
 // filter read: register-boundary layout staged by a TMA bulk copy (SMEM) or
 // read straight from global memory (BP_DIRECT: coalesced, no shared memory),
 // or chain order straight from global memory (GLOBAL), or chain order staged
-// warp by warp through the free part of the exchange buffer (LIN_STAGED)
-enum class Flt { NONE, SMEM, GLOBAL, BP_DIRECT, LIN_STAGED };
+// warp by warp through the free part of the exchange buffer (LIN_STAGED); a
+// radix-16 engine reading a filter in the radix-8 chain order (R8_STAGED) or
+// the radix-8 register-boundary order (R8BP_STAGED), staged the same way
+enum class Flt { NONE, SMEM, GLOBAL, BP_DIRECT, LIN_STAGED, R8_STAGED, R8BP_STAGED };
 
 __host__ __device__ constexpr int ilog2c(long long n) { return n <= 1 ? 0 : 1 + ilog2c(n / 2); }
 
@@ -387,6 +389,154 @@ __device__ __forceinline__ int lane_natural(int lane)
 // launches lose no launch latency.  Measured on B200, n = 1024 R16_BPERM, four
 // or more input sets in turn (> 3x L2): batch 1024 10.6 -> 9.5 us, 4096 24.5 ->
 // 22.4 us, 16384 71.9 -> 70.2 us per launch; no change for a single launch.
+// ---------------------------------------------------------------------------
+// A filter in another chain's layout.  Every layout of a power-of-two n is a
+// permutation of the index bits: chain position -> natural frequency reverses
+// the chain's digit groups (chain_natural), the register-boundary order moves
+// the last digit to the top.  So the map from this engine's chain position p
+// to the index q of the same frequency in the radix-8 layouts (the reference's
+// mixedrev order, fufft.cuh:1757-1772 with the filter permuted as in
+// verify_kernel.cpp:145-156, and its register-boundary order) is a bit
+// permutation: q = OR of sigma(b) over the set bits b of p, all known at
+// compile time.
+template<class C> __host__ __device__ constexpr int chain_nat_c(int p)
+{
+   int out = 0, pos = ilog2c(C::N), op = 0;
+   for(int k = 0; k < C::NP; ++k) {
+      const int w = ilog2c(C::radix(k));
+      pos -= w;
+      out |= ((p >> pos) & ((1 << w) - 1)) << op;
+      op += w;
+   }
+   return out;
+}
+template<class C> __host__ __device__ constexpr int chain_pos_c(int nu)   // inverse of chain_nat_c
+{
+   int p = 0, pos = ilog2c(C::N), op = 0;
+   for(int k = 0; k < C::NP; ++k) {
+      const int w = ilog2c(C::radix(k));
+      pos -= w;
+      p |= ((nu >> op) & ((1 << w) - 1)) << pos;
+      op += w;
+   }
+   return p;
+}
+
+// Staging plan of one warp's 512 filter values for the radix-16 engine (each
+// lane holds chain positions 16*l + k of the warp's 512): the low 9 bits of p
+// are the warp's own.  Bit B0 of p lands on bit 0 of q, so positions p and
+// p | (1 << B0) are one 16-byte load.  Of the other 8 low bits, 5 index the
+// lanes and 3 the loads of a lane, picked at compile time so that the
+// exchange-slot stores of a load are free of bank conflicts and each group of
+// lanes reads whole 32-byte sectors (bit 1 of q among the lane bits).
+template<class C, bool BP> struct R8Perm {
+   static constexpr int N = C::N, LB = ilog2c(N);
+   using C8 = Chain2<1, N, 8>;
+   __host__ __device__ static constexpr int map(int p)   // this chain's position -> radix-8 layout index
+   {
+      const int q = chain_pos_c<C8>(chain_nat_c<C>(p));
+      return BP ? (q >> 3) + (q & 7) * (N / 8) : q;
+   }
+   __host__ __device__ static constexpr int sig(int b) { return ilog2c(map(1 << b)); }
+   __host__ __device__ static constexpr int slot(int p)   // float2 slot of local position p (swizzled float4 rows)
+   {
+      return 2 * ((p >> 1) ^ ((p >> 4) & 7)) + (p & 1);
+   }
+   struct Plan {
+      int b0;
+      int lane[5];
+      int hi[3];
+   };
+   __host__ __device__ static constexpr int b0()
+   {
+      int r = -1;
+      for(int b = 0; b < LB; ++b)
+         if(sig(b) == 0) r = b;
+      return r;
+   }
+   // bank-conflict degree (sum over the 16 stores of a lane of the worst bank pair's count)
+   __host__ __device__ static constexpr int cost(const int (&lane)[5], const int (&hi)[3], int z)
+   {
+      int tot = 0;
+      for(int i = 0; i < 8; ++i)
+         for(int half = 0; half < 2; ++half) {
+            int cnt[16] = {};
+            int worst = 2;
+            for(int l = 0; l < 32; ++l) {
+               int p = half << z;
+               for(int t = 0; t < 5; ++t) p |= ((l >> t) & 1) << lane[t];
+               for(int t = 0; t < 3; ++t) p |= ((i >> t) & 1) << hi[t];
+               const int c = ++cnt[slot(p) & 15];
+               worst = c > worst ? c : worst;
+            }
+            tot += worst;
+         }
+      return tot;
+   }
+   __host__ __device__ static constexpr Plan plan()
+   {
+      Plan best{b0(), {0, 0, 0, 0, 0}, {0, 0, 0}};
+      int free_[8] = {}, nf = 0;
+      for(int b = 0; b < 9; ++b)
+         if(b != best.b0) free_[nf++] = b;
+      int best_cost = 1 << 30;
+      for(int m = 0; m < 256; ++m) {   // 5 of the 8 free bits for the lanes
+         int pc = 0;
+         for(int t = 0; t < 8; ++t) pc += (m >> t) & 1;
+         if(pc != 5) continue;
+         int lane[5] = {}, hi[3] = {}, nl = 0, nh = 0;
+         bool q1 = false;
+         for(int t = 0; t < 8; ++t) {
+            if((m >> t) & 1) {
+               lane[nl++] = free_[t];
+               q1 = q1 || sig(free_[t]) == 1;
+            } else {
+               hi[nh++] = free_[t];
+            }
+         }
+         const int c = cost(lane, hi, best.b0) * 2 + (q1 ? 0 : 1);
+         if(c < best_cost) {
+            best_cost = c;
+            for(int t = 0; t < 5; ++t) best.lane[t] = lane[t];
+            for(int t = 0; t < 3; ++t) best.hi[t] = hi[t];
+         }
+      }
+      return best;
+   }
+   // everything the kernel needs, as one constant (evaluated at compile time)
+   struct Tables {
+      int b0;
+      int lane[5];       // local position bit of lane bit t
+      int sig_lane[5];   // its layout-index bit
+      int sig_w[8];      // layout-index bit of warp bit t (position bit 9 + t)
+      int qh[8];         // layout-index bits of load i
+      int s0[8], s1[8];  // exchange slots of load i's two values (XOR with the lane's own)
+   };
+   __host__ __device__ static constexpr Tables tables()
+   {
+      const Plan P = plan();
+      Tables tb{};
+      tb.b0 = P.b0;
+      for(int t = 0; t < 5; ++t) {
+         tb.lane[t] = P.lane[t];
+         tb.sig_lane[t] = sig(P.lane[t]);
+      }
+      for(int t = 0; t < 8; ++t) tb.sig_w[t] = 9 + t < LB ? sig(9 + t) : 0;
+      for(int i = 0; i < 8; ++i) {
+         int hp = 0;
+         for(int t = 0; t < 3; ++t) hp |= ((i >> t) & 1) << P.hi[t];
+         int q = 0;
+         for(int b = 0; b < LB; ++b)
+            if((hp >> b) & 1) q |= 1 << sig(b);
+         tb.qh[i] = q;
+         tb.s0[i] = slot(hp);
+         tb.s1[i] = slot(hp | (1 << P.b0));
+      }
+      return tb;
+   }
+   static_assert(LB >= 9 && b0() >= 0 && b0() < 9, "bit 0 of the layout index comes from a warp-local bit");
+};
+
 #ifndef FUFFT_PDL
 #define FUFFT_PDL 1
 #endif
@@ -664,6 +814,48 @@ struct ConvKernel {
                   f[2 * i + 1] = make_float2(v.z, v.w);
                }
                __syncwarp();                 // before the first inverse exchange reuses the slots
+            } else if constexpr(FLT == Flt::R8_STAGED || FLT == Flt::R8BP_STAGED) {
+               // The same staging for a filter in a radix-8 layout: the warp's
+               // 512 values sit at q = map(512 w + local p) -- a bit
+               // permutation -- so each lane loads 16-byte pairs of its plan's
+               // positions, stores them as float2 into the row-major swizzled
+               // rows of LIN_STAGED, and reads its 16 consecutive positions back.
+               static_assert(!FBFP && T >= 32 && C::H == 1 && R == 16, "1-D fp32 radix-16 engine");
+               static_assert(warp_local_exchange<C, C::NP - 2>(), "warp-local last exchange");
+               using PM = R8Perm<C, FLT == Flt::R8BP_STAGED>;
+               constexpr typename PM::Tables TB = PM::tables();
+               const int w = lane >> 5, l = lane & 31;
+               int pl = 0, ql = 0;
+#pragma unroll
+               for(int t = 0; t < 5; ++t) {
+                  pl |= ((l >> t) & 1) << TB.lane[t];
+                  ql |= ((l >> t) & 1) << TB.sig_lane[t];
+               }
+#pragma unroll
+               for(int t = 0; t < PM::LB - 9; ++t) ql |= ((w >> t) & 1) << TB.sig_w[t];
+               // ql and qh[i] have disjoint bits: one base pointer, constant
+               // offsets; slot() is XOR-linear in p
+               const float2* fl = static_cast<const float2*>(args.b) + (size_t)filter_off(args, tr) + ql;
+               float2* S2 = X + off + 512 * w;
+               const int sl = PM::slot(pl);
+               __syncwarp();                 // every lane is past its last forward read
+#pragma unroll
+               for(int i = 0; i < 8; ++i) {
+                  const float4 v = active ? __ldg(reinterpret_cast<const float4*>(fl + TB.qh[i]))
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+                  S2[sl ^ TB.s0[i]] = make_float2(v.x, v.y);
+                  S2[sl ^ TB.s1[i]] = make_float2(v.z, v.w);
+               }
+               __syncwarp();
+               const float4* S = reinterpret_cast<const float4*>(S2);
+#pragma unroll
+               for(int i = 0; i < 8; ++i) {
+                  const int q = 8 * l + i;
+                  const float4 v = S[q ^ ((q >> 3) & 7)];
+                  f[2 * i] = make_float2(v.x, v.y);
+                  f[2 * i + 1] = make_float2(v.z, v.w);
+               }
+               __syncwarp();                 // before the first inverse exchange reuses the slots
             } else if constexpr(FLT == Flt::SMEM) {
                mbar_wait(&fbar, 0, args.status);
                if constexpr(FBFP) {
@@ -810,7 +1002,8 @@ constexpr int CONV_DIRECT_MIN_N = FUFFT_CONV_DIRECT_MIN_N;
 template<class C, In IN, Out OUT, Flt FLT> constexpr int resident_for()
 {
    return (((IN == In::C32 && OUT == Out::C32) || (IN == In::REAL2 && OUT == Out::REAL2)) &&
-           (FLT == Flt::BP_DIRECT || FLT == Flt::LIN_STAGED) && C::R == 16 && C::N >= CONV_DIRECT_MIN_N)
+           (FLT == Flt::BP_DIRECT || FLT == Flt::LIN_STAGED || FLT == Flt::R8_STAGED || FLT == Flt::R8BP_STAGED) &&
+           C::R == 16 && C::N >= CONV_DIRECT_MIN_N)
              ? FUFFT_RESIDENT_THREADS_CONV_DIRECT
         : (IN == In::C32 && OUT == Out::C32 && C::H == 1 && C::R == 8 && C::N >= CONV_DIRECT_MIN_N)
              ? FUFFT_RESIDENT_THREADS_R8

@@ -336,12 +336,53 @@ fufft_status launch_lin_staged(int n, const ConvArgs& a, cudaStream_t st, int de
    }
 }
 
+// fp32 convolution with a filter in a radix-8 layout (the reference's mixedrev
+// order of fufft_pipeline_ip, or its register-boundary order) on the radix-16
+// engine: at n = 4096 three passes each way instead of four, two exchanges
+// instead of three; the filter staged per warp through a compile-time bit
+// permutation (R8Perm).  Bit k of a mask selects n = 2^k.  Measured on B200
+// (complex convolution, 1 GiB signals, median of three interleaved runs, % of
+// measured HBM, radix-16 engine / radix-8 engine): R8 1024: 76.3 / 67.3,
+// 2048: 75.2 / 65.0, 4096: 73.4 / 58.7 (512: 83.5 / 81.0, kept on radix 8);
+// R8_BPERM 2048: 73.7 / 71.9, 4096: 67.4-70.6 / 62.8-63.6 (512: 87.0 / 96.6,
+// 1024: 69.3 / 70.5, kept on radix 8).
+#ifndef FUFFT_R8_ON_R16_LIN
+#define FUFFT_R8_ON_R16_LIN ((1 << 10) | (1 << 11) | (1 << 12))
+#endif
+#ifndef FUFFT_R8_ON_R16_BP
+#define FUFFT_R8_ON_R16_BP ((1 << 11) | (1 << 12))
+#endif
+template<Mid MID, long long MASK, Flt FLT>
+fufft_status launch_r8_on_r16(int n, const ConvArgs& a, cudaStream_t st, int dev)
+{
+#define FUFFT_PCASE(NN)                                                                          \
+   case NN:                                                                                      \
+      if constexpr(in_mask(MASK, NN)) return launch<NN, 16, In::C32, Out::C32, MID, FLT, false>(a, st, dev); \
+      else return FUFFT_ERR_UNSUPPORTED;
+   switch(n) {
+      FUFFT_PCASE(512) FUFFT_PCASE(1024) FUFFT_PCASE(2048) FUFFT_PCASE(4096)
+   default: return FUFFT_ERR_UNSUPPORTED;
+   }
+#undef FUFFT_PCASE
+}
+
 #ifndef FUFFT_LIN_STAGED
 #define FUFFT_LIN_STAGED 1
 #endif
 template<int R, bool BFP>
 fufft_status dispatch_conv(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
 {
+   if constexpr(!BFP && R == 8) {
+      if(mid != FUFFT_MID_NONE && in_mask(bperm ? FUFFT_R8_ON_R16_BP : FUFFT_R8_ON_R16_LIN, n) &&
+         aligned(a.b, 16) && (a.filter_stride * 8) % 16 == 0) {
+         constexpr long long ML = FUFFT_R8_ON_R16_LIN, MB = FUFFT_R8_ON_R16_BP;
+         if(bperm)
+            return mid == FUFFT_MID_MULTIPLY ? launch_r8_on_r16<Mid::MUL, MB, Flt::R8BP_STAGED>(n, a, st, dev)
+                                             : launch_r8_on_r16<Mid::CONJ, MB, Flt::R8BP_STAGED>(n, a, st, dev);
+         return mid == FUFFT_MID_MULTIPLY ? launch_r8_on_r16<Mid::MUL, ML, Flt::R8_STAGED>(n, a, st, dev)
+                                          : launch_r8_on_r16<Mid::CONJ, ML, Flt::R8_STAGED>(n, a, st, dev);
+      }
+   }
    // fp32, chain-order filter (the reference's v16 / ip layouts), at least one
    // warp per transform: the direct kernel staging the filter through the
    // exchange buffer

@@ -106,9 +106,10 @@ def test_conv_broadcast_filter_and_inplace(ops, oracle):
 @pytest.mark.parametrize("lname", ["R8", "R8_BPERM"])
 def test_conv_r8_filter_paths(ops, oracle, n, lname):
     """radix-8 layouts: the register-boundary filter read from global memory
-    (R8_BPERM, 512 and 1024), the TMA-staged tile (R8_BPERM, 2048 and 4096) and the
-    chain-order filter staged per warp (R8): shared and per-transform filters,
-    both mid-ops, an odd batch (a partly filled CTA below 2048)"""
+    (R8_BPERM, 512 and 1024), the radix-16 engine with the filter staged through
+    a bit permutation (R8 1024-4096, R8_BPERM 2048 and 4096), the radix-8
+    chain-order filter staged per warp (R8, 512): shared and per-transform
+    filters, both mid-ops, an odd batch (a partly filled CTA below 2048)"""
     layout, radix, v = LAYOUTS[lname]
     batch = 7
     a, b = oracle.gen_test(n, 1, batch)
@@ -118,6 +119,27 @@ def test_conv_r8_filter_paths(ops, oracle, n, lname):
             want = oracle.conv(a, oracle.permute_dr(bb, n, radix), n, radix, mid, filter_stride=fs)
             got = _host(ops.conv(_dev(a), _dev(_filter(oracle, bb, n, radix, v)), n, layout, mid, filter_stride=fs))
             assert rel_l2(got, want) <= F32_TOL, (mid, fs)
+
+
+@pytest.mark.parametrize("n", [1024, 4096])
+def test_conv_8_byte_aligned_signal(ops, oracle, n):
+    """signal and output 8 bytes off a 16-byte boundary (the filter must be
+    16-byte aligned: the C ABI answers FUFFT_ERR_MISALIGNED otherwise)"""
+    batch = 3
+    a, b = oracle.gen_test(n, 1, batch)
+    for lname, (layout, radix, v) in LAYOUTS.items():
+        want = oracle.conv(a, oracle.permute_dr(b, n, radix), n, radix)
+        da = torch.zeros(batch * n + 1, dtype=torch.complex64, device="cuda")
+        do = torch.zeros(batch * n + 1, dtype=torch.complex64, device="cuda")
+        da[1:] = _dev(a)
+        bk = _dev(_filter(oracle, b, n, radix, v))
+        got = _host(ops.conv(da[1:], bk, n, layout, out=do[1:]))
+        assert rel_l2(got, want) <= F32_TOL, lname
+        assert do[0].item() == 0
+        db = torch.zeros(batch * n + 1, dtype=torch.complex64, device="cuda")
+        db[1:] = bk
+        with pytest.raises(RuntimeError, match="MISALIGNED"):
+            ops.conv(da[1:], db[1:], n, layout, out=do[1:])
 
 
 def test_device_filter_permute_bit_exact(ops, oracle):
