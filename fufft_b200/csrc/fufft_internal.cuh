@@ -352,18 +352,31 @@ fufft_status launch_lin_staged(int n, const ConvArgs& a, cudaStream_t st, int de
 #ifndef FUFFT_R8_ON_R16_BP
 #define FUFFT_R8_ON_R16_BP ((1 << 11) | (1 << 12))
 #endif
-template<Mid MID, long long MASK, Flt FLT>
+template<Mid MID, long long MASK, Flt FLT, In IN = In::C32, Out OUT = Out::C32>
 fufft_status launch_r8_on_r16(int n, const ConvArgs& a, cudaStream_t st, int dev)
 {
 #define FUFFT_PCASE(NN)                                                                          \
    case NN:                                                                                      \
-      if constexpr(in_mask(MASK, NN)) return launch<NN, 16, In::C32, Out::C32, MID, FLT, false>(a, st, dev); \
+      if constexpr(in_mask(MASK, NN)) return launch<NN, 16, IN, OUT, MID, FLT, false>(a, st, dev); \
       else return FUFFT_ERR_UNSUPPORTED;
    switch(n) {
       FUFFT_PCASE(512) FUFFT_PCASE(1024) FUFFT_PCASE(2048) FUFFT_PCASE(4096)
    default: return FUFFT_ERR_UNSUPPORTED;
    }
 #undef FUFFT_PCASE
+}
+
+// the two radix-8 layouts on the radix-16 engine, for one kernel family
+template<In IN, Out OUT, long long ML, long long MB>
+fufft_status dispatch_r8_on_r16(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
+{
+   if(mid == FUFFT_MID_NONE || !in_mask(bperm ? MB : ML, n) || !aligned(a.b, 16) || (a.filter_stride * 8) % 16)
+      return FUFFT_ERR_UNSUPPORTED;
+   if(bperm)
+      return mid == FUFFT_MID_MULTIPLY ? launch_r8_on_r16<Mid::MUL, MB, Flt::R8BP_STAGED, IN, OUT>(n, a, st, dev)
+                                       : launch_r8_on_r16<Mid::CONJ, MB, Flt::R8BP_STAGED, IN, OUT>(n, a, st, dev);
+   return mid == FUFFT_MID_MULTIPLY ? launch_r8_on_r16<Mid::MUL, ML, Flt::R8_STAGED, IN, OUT>(n, a, st, dev)
+                                    : launch_r8_on_r16<Mid::CONJ, ML, Flt::R8_STAGED, IN, OUT>(n, a, st, dev);
 }
 
 #ifndef FUFFT_LIN_STAGED
@@ -373,15 +386,9 @@ template<int R, bool BFP>
 fufft_status dispatch_conv(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
 {
    if constexpr(!BFP && R == 8) {
-      if(mid != FUFFT_MID_NONE && in_mask(bperm ? FUFFT_R8_ON_R16_BP : FUFFT_R8_ON_R16_LIN, n) &&
-         aligned(a.b, 16) && (a.filter_stride * 8) % 16 == 0) {
-         constexpr long long ML = FUFFT_R8_ON_R16_LIN, MB = FUFFT_R8_ON_R16_BP;
-         if(bperm)
-            return mid == FUFFT_MID_MULTIPLY ? launch_r8_on_r16<Mid::MUL, MB, Flt::R8BP_STAGED>(n, a, st, dev)
-                                             : launch_r8_on_r16<Mid::CONJ, MB, Flt::R8BP_STAGED>(n, a, st, dev);
-         return mid == FUFFT_MID_MULTIPLY ? launch_r8_on_r16<Mid::MUL, ML, Flt::R8_STAGED>(n, a, st, dev)
-                                          : launch_r8_on_r16<Mid::CONJ, ML, Flt::R8_STAGED>(n, a, st, dev);
-      }
+      const fufft_status s =
+         dispatch_r8_on_r16<In::C32, Out::C32, FUFFT_R8_ON_R16_LIN, FUFFT_R8_ON_R16_BP>(n, mid, bperm, a, st, dev);
+      if(s != FUFFT_ERR_UNSUPPORTED) return s;
    }
    // fp32, chain-order filter (the reference's v16 / ip layouts), at least one
    // warp per transform: the direct kernel staging the filter through the

@@ -196,6 +196,33 @@ def test_r2_two_for_one(ops, oracle, key):
     assert rel_l2(_host(ur), want_u) <= F32_TOL and rel_l2(_host(vr), want_v) <= F32_TOL
 
 
+@pytest.mark.parametrize("n", [512, 1024, 2048, 4096])
+@pytest.mark.parametrize("lname", list(LAYOUTS))
+def test_r2_every_layout_and_filter_path(ops, oracle, n, lname):
+    """two-for-one real convolution in every filter layout: the radix-8 layouts
+    on the radix-16 engine (bit-permutation staging, n >= 1024 / 2048), the
+    radix-16 chain order staged per warp, the register-boundary order read
+    directly; both mid-ops, per-transform and shared filters"""
+    layout, radix, v = LAYOUTS[lname]
+    batch = 5
+    rng = np.random.default_rng(n + radix + v)
+    xr = rng.standard_normal(batch * n).astype(np.float32)
+    yr = rng.standard_normal(batch * n).astype(np.float32)
+    _, b = oracle.gen_test(n, 1, batch)
+    for mid in (MID_MULTIPLY, MID_CONJ):
+        for fs in (n, 0):
+            bb = b if fs else b[:n]
+            b_dr = oracle.permute_dr(bb, n, radix)
+            want_u, want_v = oracle.conv_r2(xr, yr, b_dr, n, radix, filter_stride=fs)
+            bk = oracle.bperm(b_dr, n, radix) if v > 1 else b_dr
+            ur, vr = ops.conv_r2(_dev(xr), _dev(yr), _dev(bk), n, layout, mid, filter_stride=fs)
+            if mid == MID_CONJ:   # the oracle's two-for-one applies the multiply; conj through the complex form
+                a = (xr + 1j * yr).astype(np.complex64)
+                w = oracle.conv(a, b_dr, n, radix, MID_CONJ, filter_stride=fs)
+                want_u, want_v = w.real.astype(np.float32), w.imag.astype(np.float32)
+            assert rel_l2(_host(ur), want_u) <= F32_TOL and rel_l2(_host(vr), want_v) <= F32_TOL, (mid, fs)
+
+
 # one-pass kernel: even n <= 8192 (powers of two and not); two passes: odd n, n > 8192
 @pytest.mark.parametrize("n", [2, 16, 256, 512, 1024, 2048, 3000, 4096, 8192, 999, 16384])
 def test_bfp_pack_bit_exact_and_unpack(ops, oracle, n):
