@@ -35,8 +35,8 @@ namespace fufft {
 // SPEC_BP: the same spectrum in register-boundary order, position R*lane + k
 // stored at lane + k*T (the bperm filter map) -- coalesced for every warp access
 // Out::NAT: the spectrum in natural order (plain c2c transform, no inverse).
-enum class In { C32, BFP, REAL2, SPEC, SPEC_BP };
-enum class Out { C32, BFP, REAL2, SPEC, SPEC_BP, NAT };
+enum class In { C32, BFP, REAL2, SPEC, SPEC_BP, SPEC_R8, SPEC_R8BP };
+enum class Out { C32, BFP, REAL2, SPEC, SPEC_BP, NAT, SPEC_R8, SPEC_R8BP };
 enum class Mid { NONE, MUL, CONJ };        // pointwise operation between the transforms
 // filter read: register-boundary layout staged by a TMA bulk copy (SMEM) or
 // read straight from global memory (BP_DIRECT: coalesced, no shared memory),
@@ -537,6 +537,9 @@ template<class C, bool BP> struct R8Perm {
    static_assert(LB >= 9 && b0() >= 0 && b0() < 9, "bit 0 of the layout index comes from a warp-local bit");
 };
 
+#ifndef FUFFT_SPEC_STAGED
+#define FUFFT_SPEC_STAGED 1
+#endif
 #ifndef FUFFT_PDL
 #define FUFFT_PDL 1
 #endif
@@ -550,8 +553,15 @@ struct ConvKernel {
    // product of the input and filter scales enters only the output scale
    // (a convolution is linear), saving the multiplies of the dequantisation
    static constexpr bool FOLD = IN == In::BFP && OUT == Out::BFP;
-   static constexpr bool SPEC_IN = IN == In::SPEC || IN == In::SPEC_BP;
-   static constexpr bool SPEC_OUT = OUT == Out::SPEC || OUT == Out::SPEC_BP;
+   static constexpr bool SPEC_IN = IN == In::SPEC || IN == In::SPEC_BP || IN == In::SPEC_R8 || IN == In::SPEC_R8BP;
+   static constexpr bool SPEC_OUT =
+      OUT == Out::SPEC || OUT == Out::SPEC_BP || OUT == Out::SPEC_R8 || OUT == Out::SPEC_R8BP;
+   // radix-16 chain-order spectra move through the warp's exchange slots
+   // (coalesced 16-byte accesses) when a transform has whole warps of one
+   // dimension: forward +50-68%, apply +26-35% at n = 512..4096 (B200,
+   // interleaved A/B); radix-8 rows (64 bytes per thread) measured 4-13%
+   // slower staged and keep the direct 16-byte loads
+   static constexpr bool SPEC_ROWS = FUFFT_SPEC_STAGED && R == 16 && T >= 32 && C::H == 1;
    static constexpr bool HAS_FILTER = (MID != Mid::NONE) && !SPEC_OUT;
    static constexpr int FELEM = FBFP ? 4 : 8;
    static constexpr size_t X_BYTES = (size_t)CPB * N * sizeof(float2);
@@ -572,6 +582,120 @@ struct ConvKernel {
       if constexpr(SPEC_IN)
          if(args.grid_filters > 0) return (t % args.grid_filters) * N;
       return t * args.filter_stride;
+   }
+
+   // ---- a warp's 32*R consecutive chain positions <-> each lane's R
+   // consecutive ones, through the warp's own exchange slots Xw (free between
+   // the last forward read and the first inverse write: the last exchange of
+   // each direction is warp-local).  16-byte slot q sits at q ^ ((q >> 3) &
+   // 7): conflict-free for the coalesced side and for the row side.
+   __device__ __forceinline__ static void rows_in(const float2* src, float2* Xw, int l, bool active, float2 (&v)[R])
+   {
+      constexpr int RV = R / 2;
+      float4* S = reinterpret_cast<float4*>(Xw);
+      const float4* g = reinterpret_cast<const float4*>(src);
+      __syncwarp();
+#pragma unroll
+      for(int i = 0; i < RV; ++i) {
+         const float4 w = active ? __ldg(g + l + 32 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+         S[32 * i + (l ^ (((l >> 3) + 4 * i) & 7))] = w;
+      }
+      __syncwarp();
+#pragma unroll
+      for(int i = 0; i < RV; ++i) {
+         const int q = RV * l + i;
+         const float4 w = S[q ^ ((q >> 3) & 7)];
+         v[2 * i] = make_float2(w.x, w.y);
+         v[2 * i + 1] = make_float2(w.z, w.w);
+      }
+      __syncwarp();
+   }
+   __device__ __forceinline__ static void rows_out(const float2 (&v)[R], float2* Xw, float2* dst, int l)
+   {
+      constexpr int RV = R / 2;
+      float4* S = reinterpret_cast<float4*>(Xw);
+      float4* g = reinterpret_cast<float4*>(dst);
+      __syncwarp();
+#pragma unroll
+      for(int i = 0; i < RV; ++i) {
+         const int q = RV * l + i;
+         S[q ^ ((q >> 3) & 7)] = make_float4(v[2 * i].x, v[2 * i].y, v[2 * i + 1].x, v[2 * i + 1].y);
+      }
+      __syncwarp();
+#pragma unroll
+      for(int i = 0; i < RV; ++i) st_stream(g + l + 32 * i, S[32 * i + (l ^ (((l >> 3) + 4 * i) & 7))]);
+      __syncwarp();
+   }
+   // ---- the same for a radix-8 layout (R8Perm): this warp's 512 positions
+   // sit at q = map(512 w + local p) of the transform starting at `base`
+   template<bool BP>
+   __device__ __forceinline__ static void perm_in(const float2* base, float2* Xw, int lane, bool active,
+                                                  float2 (&v)[R])
+   {
+      using PM = R8Perm<C, BP>;
+      constexpr typename PM::Tables TB = PM::tables();
+      const int w = lane >> 5, l = lane & 31;
+      int pl = 0, ql = 0;
+#pragma unroll
+      for(int t = 0; t < 5; ++t) {
+         pl |= ((l >> t) & 1) << TB.lane[t];
+         ql |= ((l >> t) & 1) << TB.sig_lane[t];
+      }
+#pragma unroll
+      for(int t = 0; t < PM::LB - 9; ++t) ql |= ((w >> t) & 1) << TB.sig_w[t];
+      // ql and qh[i] have disjoint bits: one base pointer, constant offsets;
+      // slot() is XOR-linear in p
+      const float2* g = base + ql;
+      const int sl = PM::slot(pl);
+      __syncwarp();
+#pragma unroll
+      for(int i = 0; i < 8; ++i) {
+         const float4 x = active ? __ldg(reinterpret_cast<const float4*>(g + TB.qh[i]))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+         Xw[sl ^ TB.s0[i]] = make_float2(x.x, x.y);
+         Xw[sl ^ TB.s1[i]] = make_float2(x.z, x.w);
+      }
+      __syncwarp();
+      const float4* S = reinterpret_cast<const float4*>(Xw);
+#pragma unroll
+      for(int i = 0; i < 8; ++i) {
+         const int q = 8 * l + i;
+         const float4 x = S[q ^ ((q >> 3) & 7)];
+         v[2 * i] = make_float2(x.x, x.y);
+         v[2 * i + 1] = make_float2(x.z, x.w);
+      }
+      __syncwarp();
+   }
+   template<bool BP>
+   __device__ __forceinline__ static void perm_out(const float2 (&v)[R], float2* Xw, float2* base, int lane)
+   {
+      using PM = R8Perm<C, BP>;
+      constexpr typename PM::Tables TB = PM::tables();
+      const int w = lane >> 5, l = lane & 31;
+      int pl = 0, ql = 0;
+#pragma unroll
+      for(int t = 0; t < 5; ++t) {
+         pl |= ((l >> t) & 1) << TB.lane[t];
+         ql |= ((l >> t) & 1) << TB.sig_lane[t];
+      }
+#pragma unroll
+      for(int t = 0; t < PM::LB - 9; ++t) ql |= ((w >> t) & 1) << TB.sig_w[t];
+      float4* S = reinterpret_cast<float4*>(Xw);
+      __syncwarp();
+#pragma unroll
+      for(int i = 0; i < 8; ++i) {
+         const int q = 8 * l + i;
+         S[q ^ ((q >> 3) & 7)] = make_float4(v[2 * i].x, v[2 * i].y, v[2 * i + 1].x, v[2 * i + 1].y);
+      }
+      __syncwarp();
+      float2* g = base + ql;
+      const int sl = PM::slot(pl);
+#pragma unroll
+      for(int i = 0; i < 8; ++i) {
+         const float2 a = Xw[sl ^ TB.s0[i]], b = Xw[sl ^ TB.s1[i]];
+         st_stream(reinterpret_cast<float4*>(g + TB.qh[i]), make_float4(a.x, a.y, b.x, b.y));
+      }
+      __syncwarp();
    }
 
    template<int p>
@@ -716,6 +840,11 @@ struct ConvKernel {
          if constexpr(IN == In::SPEC_BP) {
 #pragma unroll
             for(int k = 0; k < R; ++k) x[k] = active ? __ldg(sp + lane + k * T) : make_float2(0.f, 0.f);
+         } else if constexpr(IN == In::SPEC_R8 || IN == In::SPEC_R8BP) {
+            static_assert(R == 16 && T >= 32 && C::H == 1, "radix-16 engine, whole warps per transform");
+            perm_in<IN == In::SPEC_R8BP>(sp, X + off + 512 * (lane >> 5), lane, active, x);
+         } else if constexpr(SPEC_ROWS) {
+            rows_in(sp + 32 * R * (lane >> 5), X + off + 32 * R * (lane >> 5), lane & 31, active, x);
          } else {
             const float4* sp4 = reinterpret_cast<const float4*>(sp + (size_t)lane * R);
 #pragma unroll
@@ -765,6 +894,15 @@ struct ConvKernel {
                float2* sp = static_cast<float2*>(args.out) + gbase;
 #pragma unroll
                for(int k = 0; k < R; ++k) st_stream(sp + lane + k * T, x[k]);
+            } else if constexpr(OUT == Out::SPEC_R8 || OUT == Out::SPEC_R8BP) {
+               static_assert(R == 16 && T >= 32 && C::H == 1, "radix-16 engine, whole warps per transform");
+               static_assert(warp_local_exchange<C, C::NP - 2>(), "warp-local last exchange");
+               perm_out<OUT == Out::SPEC_R8BP>(x, X + off + 512 * (lane >> 5),
+                                               static_cast<float2*>(args.out) + gbase, lane);
+            } else if constexpr(SPEC_ROWS) {
+               static_assert(warp_local_exchange<C, C::NP - 2>(), "warp-local last exchange");
+               rows_out(x, X + off + 32 * R * (lane >> 5),
+                        static_cast<float2*>(args.out) + gbase + 32 * R * (lane >> 5), lane & 31);
             } else {
                float4* sp = reinterpret_cast<float4*>(static_cast<float2*>(args.out) + gbase + (size_t)lane * R);
 #pragma unroll
@@ -782,80 +920,21 @@ struct ConvKernel {
 #pragma unroll
                for(int k = 0; k < R; ++k) f[k] = active ? __ldg(fb + k * T) : make_float2(0.f, 0.f);
             } else if constexpr(FLT == Flt::LIN_STAGED) {
-               // Chain-order filter (the reference's mixedrev16 layout): thread
-               // lane needs the 16 consecutive values at 16*lane.  The last
-               // exchange of each direction is warp-local, so between the last
-               // forward read and the first inverse write this warp's 512
-               // exchange slots [off + 512 w, + 512) belong to it alone: the
-               // warp stages its 512 consecutive filter values there with
-               // coalesced 16-byte loads, then reads its rows back.  16-byte
-               // slot q sits at q ^ ((q >> 3) & 7): conflict-free both ways.
-               // (Radix 8: 256 values per warp, the same swizzle; each quarter-warp
-               // of the row reads covers 8 distinct 16-byte bank groups.)
+               // chain-order filter (the reference's mixedrev16 / mixedrev
+               // layouts): lane needs the R consecutive values at R*lane --
+               // staged warp by warp through its own exchange slots (rows_in)
                static_assert(!FBFP && T >= 32 && C::H == 1, "1-D fp32, at least one warp per transform");
                static_assert(warp_local_exchange<C, C::NP - 2>(), "warp-local last exchange");
-               constexpr int RV = R / 2;      // 16-byte slots per thread row
-               const int w = lane >> 5, l = lane & 31;
-               float4* S = reinterpret_cast<float4*>(X + off + 32 * R * w);
-               const float4* src = reinterpret_cast<const float4*>(static_cast<const float2*>(args.b) +
-                                                                  (size_t)filter_off(args, tr) + 32 * R * w);
-               __syncwarp();                 // every lane is past its last forward read
-#pragma unroll
-               for(int i = 0; i < RV; ++i) {
-                  const float4 v = active ? __ldg(src + l + 32 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
-                  S[32 * i + (l ^ (((l >> 3) + 4 * i) & 7))] = v;
-               }
-               __syncwarp();
-#pragma unroll
-               for(int i = 0; i < RV; ++i) {
-                  const int q = RV * l + i;
-                  const float4 v = S[q ^ ((q >> 3) & 7)];
-                  f[2 * i] = make_float2(v.x, v.y);
-                  f[2 * i + 1] = make_float2(v.z, v.w);
-               }
-               __syncwarp();                 // before the first inverse exchange reuses the slots
+               const int w = lane >> 5;
+               rows_in(static_cast<const float2*>(args.b) + (size_t)filter_off(args, tr) + 32 * R * w,
+                       X + off + 32 * R * w, lane & 31, active, f);
             } else if constexpr(FLT == Flt::R8_STAGED || FLT == Flt::R8BP_STAGED) {
-               // The same staging for a filter in a radix-8 layout: the warp's
-               // 512 values sit at q = map(512 w + local p) -- a bit
-               // permutation -- so each lane loads 16-byte pairs of its plan's
-               // positions, stores them as float2 into the row-major swizzled
-               // rows of LIN_STAGED, and reads its 16 consecutive positions back.
+               // a filter in a radix-8 layout: the warp's 512 values sit at
+               // q = map(512 w + local p), a bit permutation (perm_in)
                static_assert(!FBFP && T >= 32 && C::H == 1 && R == 16, "1-D fp32 radix-16 engine");
                static_assert(warp_local_exchange<C, C::NP - 2>(), "warp-local last exchange");
-               using PM = R8Perm<C, FLT == Flt::R8BP_STAGED>;
-               constexpr typename PM::Tables TB = PM::tables();
-               const int w = lane >> 5, l = lane & 31;
-               int pl = 0, ql = 0;
-#pragma unroll
-               for(int t = 0; t < 5; ++t) {
-                  pl |= ((l >> t) & 1) << TB.lane[t];
-                  ql |= ((l >> t) & 1) << TB.sig_lane[t];
-               }
-#pragma unroll
-               for(int t = 0; t < PM::LB - 9; ++t) ql |= ((w >> t) & 1) << TB.sig_w[t];
-               // ql and qh[i] have disjoint bits: one base pointer, constant
-               // offsets; slot() is XOR-linear in p
-               const float2* fl = static_cast<const float2*>(args.b) + (size_t)filter_off(args, tr) + ql;
-               float2* S2 = X + off + 512 * w;
-               const int sl = PM::slot(pl);
-               __syncwarp();                 // every lane is past its last forward read
-#pragma unroll
-               for(int i = 0; i < 8; ++i) {
-                  const float4 v = active ? __ldg(reinterpret_cast<const float4*>(fl + TB.qh[i]))
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
-                  S2[sl ^ TB.s0[i]] = make_float2(v.x, v.y);
-                  S2[sl ^ TB.s1[i]] = make_float2(v.z, v.w);
-               }
-               __syncwarp();
-               const float4* S = reinterpret_cast<const float4*>(S2);
-#pragma unroll
-               for(int i = 0; i < 8; ++i) {
-                  const int q = 8 * l + i;
-                  const float4 v = S[q ^ ((q >> 3) & 7)];
-                  f[2 * i] = make_float2(v.x, v.y);
-                  f[2 * i + 1] = make_float2(v.z, v.w);
-               }
-               __syncwarp();                 // before the first inverse exchange reuses the slots
+               perm_in<FLT == Flt::R8BP_STAGED>(static_cast<const float2*>(args.b) + (size_t)filter_off(args, tr),
+                                                X + off + 512 * (lane >> 5), lane, active, f);
             } else if constexpr(FLT == Flt::SMEM) {
                mbar_wait(&fbar, 0, args.status);
                if constexpr(FBFP) {

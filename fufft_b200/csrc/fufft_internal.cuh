@@ -283,31 +283,6 @@ fufft_status dispatch_mid(int n, fufft_midop mid, bool bperm, const ConvArgs& a,
    return FUFFT_ERR_INVALID_ARG;
 }
 
-// split apply: the spectrum comes in the layout family of the filter --
-// register-boundary order with the TMA-staged bperm filter, chain order with
-// the chain-order filter
-#ifndef FUFFT_APPLY_FILTER_DIRECT
-#define FUFFT_APPLY_FILTER_DIRECT 1
-#endif
-constexpr Flt APPLY_FLT = FUFFT_APPLY_FILTER_DIRECT ? Flt::BP_DIRECT : Flt::SMEM;
-
-template<int R, Out OUT>
-fufft_status dispatch_apply(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
-{
-   switch(mid) {
-   case FUFFT_MID_NONE:
-      return bperm ? launch_n<R, In::SPEC_BP, OUT, Mid::NONE, Flt::NONE, false>(n, a, st, dev)
-                   : launch_n<R, In::SPEC, OUT, Mid::NONE, Flt::NONE, false>(n, a, st, dev);
-   case FUFFT_MID_MULTIPLY:
-      return bperm ? launch_n<R, In::SPEC_BP, OUT, Mid::MUL, APPLY_FLT, false>(n, a, st, dev)
-                   : launch_n<R, In::SPEC, OUT, Mid::MUL, Flt::GLOBAL, false>(n, a, st, dev);
-   case FUFFT_MID_CONJ_MULTIPLY:
-      return bperm ? launch_n<R, In::SPEC_BP, OUT, Mid::CONJ, APPLY_FLT, false>(n, a, st, dev)
-                   : launch_n<R, In::SPEC, OUT, Mid::CONJ, Flt::GLOBAL, false>(n, a, st, dev);
-   }
-   return FUFFT_ERR_INVALID_ARG;
-}
-
 // fp32 / BFP convolution.  Measured on B200 (N = 512..8192, 1 GiB signal):
 // the direct kernel (fufft_conv.cuh) is fastest whenever the filter arrives in
 // the register-boundary layout (TMA bulk prefetch) and for BFP; the
@@ -377,6 +352,101 @@ fufft_status dispatch_r8_on_r16(int n, fufft_midop mid, bool bperm, const ConvAr
                                        : launch_r8_on_r16<Mid::CONJ, MB, Flt::R8BP_STAGED, IN, OUT>(n, a, st, dev);
    return mid == FUFFT_MID_MULTIPLY ? launch_r8_on_r16<Mid::MUL, ML, Flt::R8_STAGED, IN, OUT>(n, a, st, dev)
                                     : launch_r8_on_r16<Mid::CONJ, ML, Flt::R8_STAGED, IN, OUT>(n, a, st, dev);
+}
+
+// split apply: the spectrum comes in the layout family of the filter --
+// register-boundary order with the register-boundary filter, chain order with
+// the chain-order filter
+#ifndef FUFFT_APPLY_FILTER_DIRECT
+#define FUFFT_APPLY_FILTER_DIRECT 1
+#endif
+constexpr Flt APPLY_FLT = FUFFT_APPLY_FILTER_DIRECT ? Flt::BP_DIRECT : Flt::SMEM;
+// radix-8 spectra and filters (the reference's fufft_pipeline_fwd / _apply
+// layouts, fufft.cuh:1343-1407) on the radix-16 engine, for n = 2^k with bit
+// k of the mask: spectra and filters staged per warp through the bit
+// permutation (R8Perm).  Measured on B200 (1 GiB, % of HBM at 16 B/pt
+// forward and 24 B/pt apply, radix-16 engine / radix-8 engine, the two
+// builds interleaved kernel by kernel in one process): forward R8 512: 99 /
+// 82, 1024: 88 / 58, 2048: 88 / 53, 4096: 93 / 42; forward R8_BPERM 4096:
+// 86 / 55 (1024, 2048: 85 / 89, 75 / 79, kept on radix 8); apply R8 4096:
+// 82 / 59 (1024, 2048: 87 / 90, 72 / 80); apply R8_BPERM (spectrum and
+// filter read directly by the radix-8 engine) 74 / 107, 64 / 108, 63 / 93.
+#ifndef FUFFT_FWD_R8_ON_R16
+#define FUFFT_FWD_R8_ON_R16 ((1 << 9) | (1 << 10) | (1 << 11) | (1 << 12))
+#endif
+#ifndef FUFFT_FWD_R8BP_ON_R16
+#define FUFFT_FWD_R8BP_ON_R16 (1 << 12)
+#endif
+#ifndef FUFFT_APPLY_R8_ON_R16
+#define FUFFT_APPLY_R8_ON_R16 (1 << 12)
+#endif
+#ifndef FUFFT_APPLY_R8BP_ON_R16
+#define FUFFT_APPLY_R8BP_ON_R16 0
+#endif
+#ifndef FUFFT_APPLY_LIN_STAGED
+#define FUFFT_APPLY_LIN_STAGED 1
+#endif
+
+template<int R, Out OUT>
+fufft_status dispatch_apply(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
+{
+   const bool filt_ok = aligned(a.b, 16) && (a.filter_stride * 8) % 16 == 0;
+   if constexpr(R == 8) {
+      constexpr long long M = FUFFT_APPLY_R8_ON_R16, MB = FUFFT_APPLY_R8BP_ON_R16;
+      if(bperm && in_mask(MB, n) && (mid == FUFFT_MID_NONE || filt_ok)) {
+         switch(mid) {
+         case FUFFT_MID_NONE: return launch_r8_on_r16<Mid::NONE, MB, Flt::NONE, In::SPEC_R8BP, OUT>(n, a, st, dev);
+         case FUFFT_MID_MULTIPLY:
+            return launch_r8_on_r16<Mid::MUL, MB, Flt::R8BP_STAGED, In::SPEC_R8BP, OUT>(n, a, st, dev);
+         case FUFFT_MID_CONJ_MULTIPLY:
+            return launch_r8_on_r16<Mid::CONJ, MB, Flt::R8BP_STAGED, In::SPEC_R8BP, OUT>(n, a, st, dev);
+         }
+         return FUFFT_ERR_INVALID_ARG;
+      }
+      if(!bperm && in_mask(M, n) && (mid == FUFFT_MID_NONE || filt_ok)) {
+         switch(mid) {
+         case FUFFT_MID_NONE: return launch_r8_on_r16<Mid::NONE, M, Flt::NONE, In::SPEC_R8, OUT>(n, a, st, dev);
+         case FUFFT_MID_MULTIPLY:
+            return launch_r8_on_r16<Mid::MUL, M, Flt::R8_STAGED, In::SPEC_R8, OUT>(n, a, st, dev);
+         case FUFFT_MID_CONJ_MULTIPLY:
+            return launch_r8_on_r16<Mid::CONJ, M, Flt::R8_STAGED, In::SPEC_R8, OUT>(n, a, st, dev);
+         }
+         return FUFFT_ERR_INVALID_ARG;
+      }
+   }
+   // radix-16 chain-order filter with whole warps per transform: staged per
+   // warp (the spectrum too: SPEC_ROWS)
+   if constexpr(FUFFT_APPLY_LIN_STAGED && R == 16) {
+      if(!bperm && mid != FUFFT_MID_NONE && n >= 32 * R && n <= max_n(R) && filt_ok)
+         return mid == FUFFT_MID_MULTIPLY ? launch_lin_staged<R, In::SPEC, OUT, Mid::MUL>(n, a, st, dev)
+                                          : launch_lin_staged<R, In::SPEC, OUT, Mid::CONJ>(n, a, st, dev);
+   }
+   switch(mid) {
+   case FUFFT_MID_NONE:
+      return bperm ? launch_n<R, In::SPEC_BP, OUT, Mid::NONE, Flt::NONE, false>(n, a, st, dev)
+                   : launch_n<R, In::SPEC, OUT, Mid::NONE, Flt::NONE, false>(n, a, st, dev);
+   case FUFFT_MID_MULTIPLY:
+      return bperm ? launch_n<R, In::SPEC_BP, OUT, Mid::MUL, APPLY_FLT, false>(n, a, st, dev)
+                   : launch_n<R, In::SPEC, OUT, Mid::MUL, Flt::GLOBAL, false>(n, a, st, dev);
+   case FUFFT_MID_CONJ_MULTIPLY:
+      return bperm ? launch_n<R, In::SPEC_BP, OUT, Mid::CONJ, APPLY_FLT, false>(n, a, st, dev)
+                   : launch_n<R, In::SPEC, OUT, Mid::CONJ, Flt::GLOBAL, false>(n, a, st, dev);
+   }
+   return FUFFT_ERR_INVALID_ARG;
+}
+
+// forward transform to a spectrum in the layout's order (fwd, fwd_r2, filter
+// preparation); radix-8 layouts on the radix-16 engine as for the apply
+template<int R, In IN>
+fufft_status dispatch_fwd(int n, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
+{
+   if constexpr(R == 8) {
+      constexpr long long M = FUFFT_FWD_R8_ON_R16, MB = FUFFT_FWD_R8BP_ON_R16;
+      if(bperm && in_mask(MB, n)) return launch_r8_on_r16<Mid::NONE, MB, Flt::NONE, IN, Out::SPEC_R8BP>(n, a, st, dev);
+      if(!bperm && in_mask(M, n)) return launch_r8_on_r16<Mid::NONE, M, Flt::NONE, IN, Out::SPEC_R8>(n, a, st, dev);
+   }
+   return bperm ? launch_n<R, IN, Out::SPEC_BP, Mid::NONE, Flt::NONE, false>(n, a, st, dev)
+                : launch_n<R, IN, Out::SPEC, Mid::NONE, Flt::NONE, false>(n, a, st, dev);
 }
 
 #ifndef FUFFT_LIN_STAGED

@@ -11,8 +11,7 @@ fufft_status family_apply_r2_r16(int n, fufft_midop mid, bool bperm, const ConvA
 fufft_status family_fwd_r2_r16(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
 {
    (void)mid;
-   return bperm ? launch_n<16, In::REAL2, Out::SPEC_BP, Mid::NONE, Flt::NONE, false>(n, a, st, dev)
-                : launch_n<16, In::REAL2, Out::SPEC, Mid::NONE, Flt::NONE, false>(n, a, st, dev);
+   return dispatch_fwd<16, In::REAL2>(n, bperm, a, st, dev);
 }
 }  // namespace host
 }  // namespace fufft

@@ -5,8 +5,7 @@ namespace host {
 fufft_status family_fwd_r16(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
 {
    (void)mid;
-   return bperm ? launch_n<16, In::C32, Out::SPEC_BP, Mid::NONE, Flt::NONE, false>(n, a, st, dev)
-                : launch_n<16, In::C32, Out::SPEC, Mid::NONE, Flt::NONE, false>(n, a, st, dev);
+   return dispatch_fwd<16, In::C32>(n, bperm, a, st, dev);
 }
 }  // namespace host
 }  // namespace fufft
