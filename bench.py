@@ -681,9 +681,10 @@ def run_ncu_all():
     call("conv fp32 R16_BPERM (register-boundary filter, read directly)", lambda: ops.conv(a, b, n, ops.LAYOUT_R16_BPERM, out=o), pts, 24 * pts)
     call("conv fp32 R16 (linear mixedrev16 filter, staged per warp)", lambda: ops.conv(a, b, n, ops.LAYOUT_R16, out=o),
          pts, 24 * pts)
-    call("conv fp32 R8_BPERM", lambda: ops.conv(a, b, n, ops.LAYOUT_R8_BPERM, out=o), pts, 24 * pts)
-    call("conv fp32 R8 (linear mixedrev filter, staged per warp)", lambda: ops.conv(a, b, n, ops.LAYOUT_R8, out=o),
-         pts, 24 * pts)
+    call("conv fp32 R8_BPERM (radix-16 engine, filter staged through the bit permutation)",
+         lambda: ops.conv(a, b, n, ops.LAYOUT_R8_BPERM, out=o), pts, 24 * pts)
+    call("conv fp32 R8 (linear mixedrev filter, radix-16 engine, bit-permutation staging)",
+         lambda: ops.conv(a, b, n, ops.LAYOUT_R8, out=o), pts, 24 * pts)
     call("conv fp32 R16_BPERM conj-multiply", lambda: ops.conv(a, b, n, ops.LAYOUT_R16_BPERM, ops.MID_CONJ_MULTIPLY, out=o), pts, 24 * pts)
     aq, as_ = ops.bfp_pack(a, n)
     torch.cuda.synchronize()
@@ -700,10 +701,23 @@ def run_ncu_all():
     torch.cuda.synchronize()
     man.append(("fwd (spectrum for apply)", 1, pts, 16 * pts))
     call("apply (split apply, R16_BPERM)", lambda: ops.apply(spec, b, n, ops.LAYOUT_R16_BPERM, out=o), pts, 24 * pts)
+    # the reference's own split layout (radix-8 chain order) and the radix-16 chain order
+    call("fwd (split forward, R8 spectrum: radix-16 engine, bit-permutation staging)",
+         lambda: ops.fwd(a, n, ops.LAYOUT_R8), pts, 16 * pts)
+    spec8 = ops.fwd(a, n, ops.LAYOUT_R8)
+    torch.cuda.synchronize()
+    man.append(("fwd (R8 spectrum for apply)", 1, pts, 16 * pts))
+    call("apply (split apply, R8 spectrum and filter)", lambda: ops.apply(spec8, b, n, ops.LAYOUT_R8, out=o),
+         pts, 24 * pts)
+    del spec8
+    call("fwd (split forward, R16 chain-order spectrum, staged per warp)", lambda: ops.fwd(a, n, ops.LAYOUT_R16),
+         pts, 16 * pts)
     xr, yr = a.real.contiguous(), a.imag.contiguous()
     torch.cuda.synchronize()
     man.append(("(torch copies of re / im)", 2, 0, 0))
     call("conv_r2 two-for-one real", lambda: ops.conv_r2(xr, yr, b, n, ops.LAYOUT_R16_BPERM), 2 * pts, 12 * 2 * pts)
+    call("conv_r2 two-for-one real, R8 filter (the reference's layout)",
+         lambda: ops.conv_r2(xr, yr, b, n, ops.LAYOUT_R8), 2 * pts, 12 * 2 * pts)
     call("fwd_r2 (packed real pairs)", lambda: ops.fwd_r2(xr, yr, n, ops.LAYOUT_R16_BPERM), 2 * pts, 16 * pts)
     sp512 = spec[: 512 * n]
     fl = b[: 256 * n]
