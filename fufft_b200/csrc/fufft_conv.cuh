@@ -399,22 +399,24 @@ __device__ __forceinline__ int lane_natural(int lane)
 // verify_kernel.cpp:145-156, and its register-boundary order) is a bit
 // permutation: q = OR of sigma(b) over the set bits b of p, all known at
 // compile time.
-template<class C> __host__ __device__ constexpr int chain_nat_c(int p)
+// chain position p -> natural frequency for the 1-D chain of n points under
+// base radix R (the dim_radix chain), and its inverse
+__host__ __device__ constexpr int dim_nat(int p, int n, int R)
 {
-   int out = 0, pos = ilog2c(C::N), op = 0;
-   for(int k = 0; k < C::NP; ++k) {
-      const int w = ilog2c(C::radix(k));
+   int out = 0, pos = ilog2c(n), op = 0;
+   for(int k = 0; k < dim_passes(n, R); ++k) {
+      const int w = ilog2c(dim_radix(n, R, k));
       pos -= w;
       out |= ((p >> pos) & ((1 << w) - 1)) << op;
       op += w;
    }
    return out;
 }
-template<class C> __host__ __device__ constexpr int chain_pos_c(int nu)   // inverse of chain_nat_c
+__host__ __device__ constexpr int dim_pos(int nu, int n, int R)
 {
-   int p = 0, pos = ilog2c(C::N), op = 0;
-   for(int k = 0; k < C::NP; ++k) {
-      const int w = ilog2c(C::radix(k));
+   int p = 0, pos = ilog2c(n), op = 0;
+   for(int k = 0; k < dim_passes(n, R); ++k) {
+      const int w = ilog2c(dim_radix(n, R, k));
       pos -= w;
       p |= ((nu >> op) & ((1 << w) - 1)) << pos;
       op += w;
@@ -431,10 +433,13 @@ template<class C> __host__ __device__ constexpr int chain_pos_c(int nu)   // inv
 // lanes reads whole 32-byte sectors (bit 1 of q among the lane bits).
 template<class C, bool BP> struct R8Perm {
    static constexpr int N = C::N, LB = ilog2c(N);
-   using C8 = Chain2<1, N, 8>;
-   __host__ __device__ static constexpr int map(int p)   // this chain's position -> radix-8 layout index
+   // this chain's position -> radix-8 layout index.  2-D (H x W): each
+   // dimension's digits are reversed on its own (slot (r, c) holds frequency
+   // (rev_H(r), rev_W(c)) in both layouts)
+   __host__ __device__ static constexpr int map(int p)
    {
-      const int q = chain_pos_c<C8>(chain_nat_c<C>(p));
+      const int r = p / C::W, c = p % C::W;
+      const int q = dim_pos(dim_nat(r, C::H, 16), C::H, 8) * C::W + dim_pos(dim_nat(c, C::W, 16), C::W, 8);
       return BP ? (q >> 3) + (q & 7) * (N / 8) : q;
    }
    __host__ __device__ static constexpr int sig(int b) { return ilog2c(map(1 << b)); }
@@ -585,10 +590,13 @@ struct ConvKernel {
    }
 
    // ---- a warp's 32*R consecutive chain positions <-> each lane's R
-   // consecutive ones, through the warp's own exchange slots Xw (free between
-   // the last forward read and the first inverse write: the last exchange of
-   // each direction is warp-local).  16-byte slot q sits at q ^ ((q >> 3) &
-   // 7): conflict-free for the coalesced side and for the row side.
+   // consecutive ones, through the warp's own exchange slots Xw.  The last
+   // pass (stride 1, radix R) gives warp w exactly the positions [32 R w,
+   // +32 R), and the exchange into it is either warp-local or behind a
+   // barrier of the transform's threads, so between warp w's last forward
+   // read and its first inverse write no other warp touches those slots.
+   // 16-byte slot q sits at q ^ ((q >> 3) & 7): conflict-free for the
+   // coalesced side and for the row side.
    __device__ __forceinline__ static void rows_in(const float2* src, float2* Xw, int l, bool active, float2 (&v)[R])
    {
       constexpr int RV = R / 2;
@@ -896,11 +904,9 @@ struct ConvKernel {
                for(int k = 0; k < R; ++k) st_stream(sp + lane + k * T, x[k]);
             } else if constexpr(OUT == Out::SPEC_R8 || OUT == Out::SPEC_R8BP) {
                static_assert(R == 16 && T >= 32 && C::H == 1, "radix-16 engine, whole warps per transform");
-               static_assert(warp_local_exchange<C, C::NP - 2>(), "warp-local last exchange");
                perm_out<OUT == Out::SPEC_R8BP>(x, X + off + 512 * (lane >> 5),
                                                static_cast<float2*>(args.out) + gbase, lane);
             } else if constexpr(SPEC_ROWS) {
-               static_assert(warp_local_exchange<C, C::NP - 2>(), "warp-local last exchange");
                rows_out(x, X + off + 32 * R * (lane >> 5),
                         static_cast<float2*>(args.out) + gbase + 32 * R * (lane >> 5), lane & 31);
             } else {
@@ -923,16 +929,14 @@ struct ConvKernel {
                // chain-order filter (the reference's mixedrev16 / mixedrev
                // layouts): lane needs the R consecutive values at R*lane --
                // staged warp by warp through its own exchange slots (rows_in)
-               static_assert(!FBFP && T >= 32 && C::H == 1, "1-D fp32, at least one warp per transform");
-               static_assert(warp_local_exchange<C, C::NP - 2>(), "warp-local last exchange");
+               static_assert(!FBFP && T >= 32, "fp32, at least one warp per transform");
                const int w = lane >> 5;
                rows_in(static_cast<const float2*>(args.b) + (size_t)filter_off(args, tr) + 32 * R * w,
                        X + off + 32 * R * w, lane & 31, active, f);
             } else if constexpr(FLT == Flt::R8_STAGED || FLT == Flt::R8BP_STAGED) {
                // a filter in a radix-8 layout: the warp's 512 values sit at
                // q = map(512 w + local p), a bit permutation (perm_in)
-               static_assert(!FBFP && T >= 32 && C::H == 1 && R == 16, "1-D fp32 radix-16 engine");
-               static_assert(warp_local_exchange<C, C::NP - 2>(), "warp-local last exchange");
+               static_assert(!FBFP && T >= 32 && R == 16, "fp32 radix-16 engine, at least one warp per transform");
                perm_in<FLT == Flt::R8BP_STAGED>(static_cast<const float2*>(args.b) + (size_t)filter_off(args, tr),
                                                 X + off + 512 * (lane >> 5), lane, active, f);
             } else if constexpr(FLT == Flt::SMEM) {

@@ -46,7 +46,7 @@ def test_conv2d_reference_cases(ops, oracle, h, w, batch):
 
 
 SHAPES16 = [(8, 16), (16, 16), (8, 64), (64, 64), (128, 64), (64, 128), (16, 512), (512, 16), (32, 256)]
-SHAPES8 = [(8, 8), (16, 8), (32, 32), (64, 32), (8, 256), (256, 16)]
+SHAPES8 = [(8, 8), (16, 8), (16, 32), (32, 32), (64, 32), (8, 256), (256, 16)]
 
 
 @pytest.mark.parametrize("radix,h,w", [(16, h, w) for h, w in SHAPES16] + [(8, h, w) for h, w in SHAPES8])
@@ -77,6 +77,25 @@ def test_conv2d_broadcast_filter_and_device_permute(ops, oracle):
     want = oracle.conv2d(a, b2, h, w, 16, MID_MULTIPLY, filter_stride=0)
     got = ops.conv2d(_dev(a), dev_b2, h, w, ops.LAYOUT_R16_BPERM, filter_stride=0).cpu().numpy()
     assert rel_l2(got, want) <= F32_TOL
+
+
+@pytest.mark.parametrize("h,w", [(64, 64), (8, 512), (32, 16)])
+def test_conv2d_reference_layout_shared_filter(ops, oracle, h, w):
+    """the reference's 2-D filter order (radix 8 per dimension) with one filter
+    for every image, in both orders: on the radix-16 engine through the bit
+    permutation (rows of 16 or more)"""
+    batch = 5
+    rng = np.random.default_rng(h + 3 * w)
+    a = rng.uniform(0, 1, h * w * batch).astype(np.complex64)
+    b = (rng.standard_normal(h * w) + 1j * rng.standard_normal(h * w)).astype(np.complex64) / (h * w)
+    b2 = oracle.permute2d(b, h, w, 8)
+    for mid in (MID_MULTIPLY, MID_CONJ):
+        want = oracle.conv2d(a, b2, h, w, 8, mid, filter_stride=0)
+        got = ops.conv2d(_dev(a), _dev(b2), h, w, ops.LAYOUT_R8, mid, filter_stride=0).cpu().numpy()
+        assert rel_l2(got, want) <= F32_TOL, mid
+        got = ops.conv2d(_dev(a), _dev(_bperm(b2, h * w, 8)), h, w, ops.LAYOUT_R8_BPERM, mid,
+                         filter_stride=0).cpu().numpy()
+        assert rel_l2(got, want) <= F32_TOL, (mid, "bperm")
 
 
 def test_conv2d_rejects_unsupported_shape(ops):
