@@ -1075,6 +1075,12 @@ template<In IN, Out OUT> constexpr int resident_threads()
 #define FUFFT_CONV_DIRECT_MIN_N 2048
 #endif
 constexpr int CONV_DIRECT_MIN_N = FUFFT_CONV_DIRECT_MIN_N;
+// n = 1024 launches of a few waves (up to CONV_DIRECT_SMALL_POINTS points) read
+// the register-boundary filter directly at three CTAs per SM too: back-to-back
+// 4096-transform launches 22.3 -> 21.3 us (B200, four input sets in turn);
+// at 2^24 points even, at 1 GiB 1% slower, so larger launches keep the tile
+constexpr int CONV_DIRECT_SMALL_N = 1024;
+constexpr long long CONV_DIRECT_SMALL_POINTS = 1LL << 23;
 // fp32 radix-8 convolution of n >= 2048 (one transform per CTA, 256 or 512
 // threads): two or more CTAs per SM at <= 64 registers.  At the 512-thread
 // target one 512-thread CTA of 67 registers filled the SM: 16 warps, issue
@@ -1086,7 +1092,7 @@ template<class C, In IN, Out OUT, Flt FLT> constexpr int resident_for()
 {
    return (((IN == In::C32 && OUT == Out::C32) || (IN == In::REAL2 && OUT == Out::REAL2)) &&
            (FLT == Flt::BP_DIRECT || FLT == Flt::LIN_STAGED || FLT == Flt::R8_STAGED || FLT == Flt::R8BP_STAGED) &&
-           C::R == 16 && C::N >= CONV_DIRECT_MIN_N)
+           C::R == 16 && (C::N >= CONV_DIRECT_MIN_N || (FLT == Flt::BP_DIRECT && C::N == CONV_DIRECT_SMALL_N)))
              ? FUFFT_RESIDENT_THREADS_CONV_DIRECT
         : (IN == In::C32 && OUT == Out::C32 && C::H == 1 && C::R == 8 && C::N >= CONV_DIRECT_MIN_N)
              ? FUFFT_RESIDENT_THREADS_R8

@@ -261,7 +261,8 @@ fufft_status dispatch_mid(int n, fufft_midop mid, bool bperm, const ConvArgs& a,
 {
    if constexpr(FUFFT_CONV_FILTER_DIRECT && R == 16 && !FBFP &&
                 ((IN == In::C32 && OUT == Out::C32) || (FUFFT_R2_FILTER_DIRECT && IN == In::REAL2 && OUT == Out::REAL2))) {
-      if(bperm && n >= CONV_DIRECT_MIN_N && mid != FUFFT_MID_NONE)
+      const bool small = IN == In::C32 && n == CONV_DIRECT_SMALL_N && a.batch * n <= CONV_DIRECT_SMALL_POINTS;
+      if(bperm && (n >= CONV_DIRECT_MIN_N || small) && mid != FUFFT_MID_NONE)
          return mid == FUFFT_MID_MULTIPLY ? launch_n<R, IN, OUT, Mid::MUL, Flt::BP_DIRECT, FBFP>(n, a, st, dev)
                                           : launch_n<R, IN, OUT, Mid::CONJ, Flt::BP_DIRECT, FBFP>(n, a, st, dev);
    }
