@@ -731,6 +731,10 @@ def run_ncu_all():
     h = w = 64
     call("conv2d 64x64 one CTA (shared filter, read directly)",
          lambda: ops.conv2d(a, b[: h * w], h, w, ops.LAYOUT_R16_BPERM, filter_stride=0, out=o), pts, 16 * pts)
+    call("conv2d 64x64 per-image filter in the reference's radix-8 order (radix-16 engine, bit-permutation staging)",
+         lambda: ops.conv2d(a, b, h, w, ops.LAYOUT_R8, out=o), pts, 24 * pts)
+    call("conv2d 8x512 per-image filter in the reference's radix-8 order",
+         lambda: ops.conv2d(a, b, 8, 512, ops.LAYOUT_R8, out=o), pts, 24 * pts)
     call("conv2d 256x256 cluster (shared filter)", lambda: ops.conv2d(a, b[: 65536], 256, 256, ops.LAYOUT_R16_BPERM, filter_stride=0, out=o),
          pts, 16 * pts)
     n2 = 32768
