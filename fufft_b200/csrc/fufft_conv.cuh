@@ -43,8 +43,9 @@ enum class Mid { NONE, MUL, CONJ };        // pointwise operation between the tr
 // or chain order straight from global memory (GLOBAL), or chain order staged
 // warp by warp through the free part of the exchange buffer (LIN_STAGED); a
 // radix-16 engine reading a filter in the radix-8 chain order (R8_STAGED) or
-// the radix-8 register-boundary order (R8BP_STAGED), staged the same way
-enum class Flt { NONE, SMEM, GLOBAL, BP_DIRECT, LIN_STAGED, R8_STAGED, R8BP_STAGED };
+// the radix-8 register-boundary order (R8BP_STAGED), staged the same way, or
+// the register-boundary order read straight from global memory (R8BP_DIRECT)
+enum class Flt { NONE, SMEM, GLOBAL, BP_DIRECT, LIN_STAGED, R8_STAGED, R8BP_STAGED, R8BP_DIRECT };
 
 __host__ __device__ constexpr int ilog2c(long long n) { return n <= 1 ? 0 : 1 + ilog2c(n / 2); }
 
@@ -443,6 +444,16 @@ template<class C, bool BP> struct R8Perm {
       return BP ? (q >> 3) + (q & 7) * (N / 8) : q;
    }
    __host__ __device__ static constexpr int sig(int b) { return ilog2c(map(1 << b)); }
+   // do the five low lane bits (position bits 4..8) land on index bits 0 and 1?
+   __host__ __device__ static constexpr bool lanes_cover_q01()
+   {
+      bool z = false, o = false;
+      for(int b = 4; b < 9 && b < LB; ++b) {
+         z = z || sig(b) == 0;
+         o = o || sig(b) == 1;
+      }
+      return z && o;
+   }
    __host__ __device__ static constexpr int slot(int p)   // float2 slot of local position p (swizzled float4 rows)
    {
       return 2 * ((p >> 1) ^ ((p >> 4) & 7)) + (p & 1);
@@ -516,11 +527,15 @@ template<class C, bool BP> struct R8Perm {
       int sig_w[8];      // layout-index bit of warp bit t (position bit 9 + t)
       int qh[8];         // layout-index bits of load i
       int s0[8], s1[8];  // exchange slots of load i's two values (XOR with the lane's own)
+      int sig[16];       // layout-index bit of every position bit (direct reads)
+      int mapk[16];      // layout index of positions 0..15 (register k of lane 0)
    };
    __host__ __device__ static constexpr Tables tables()
    {
       const Plan P = plan();
       Tables tb{};
+      for(int b = 0; b < 16; ++b) tb.sig[b] = b < LB ? sig(b) : 0;
+      for(int k = 0; k < 16; ++k) tb.mapk[k] = map(k);
       tb.b0 = P.b0;
       for(int t = 0; t < 5; ++t) {
          tb.lane[t] = P.lane[t];
@@ -933,6 +948,27 @@ struct ConvKernel {
                const int w = lane >> 5;
                rows_in(static_cast<const float2*>(args.b) + (size_t)filter_off(args, tr) + 32 * R * w,
                        X + off + 32 * R * w, lane & 31, active, f);
+            } else if constexpr(FLT == Flt::R8BP_DIRECT) {
+               // the radix-8 register-boundary filter read straight from
+               // global memory: q = map(16 lane + k) splits into a lane part
+               // and a constant per k (map is a bit permutation), and the low
+               // lane bits land on bits 0 and 1 of q, so every four lanes read
+               // one whole 32-byte sector per load
+               // (shapes whose low lane bits miss those bits stage instead)
+               static_assert(!FBFP && T >= 32 && R == 16, "fp32 radix-16 engine, at least one warp per transform");
+               using PM = R8Perm<C, true>;
+               if constexpr(PM::lanes_cover_q01()) {
+                  constexpr typename PM::Tables TB = PM::tables();   // evaluated at compile time
+                  int ql = 0;
+#pragma unroll
+                  for(int t = 0; t + 4 < PM::LB; ++t) ql |= ((lane >> t) & 1) << TB.sig[4 + t];
+                  const float2* fb = static_cast<const float2*>(args.b) + (size_t)filter_off(args, tr) + ql;
+#pragma unroll
+                  for(int k = 0; k < R; ++k) f[k] = active ? __ldg(fb + TB.mapk[k]) : make_float2(0.f, 0.f);
+               } else {
+                  perm_in<true>(static_cast<const float2*>(args.b) + (size_t)filter_off(args, tr),
+                                X + off + 512 * (lane >> 5), lane, active, f);
+               }
             } else if constexpr(FLT == Flt::R8_STAGED || FLT == Flt::R8BP_STAGED) {
                // a filter in a radix-8 layout: the warp's 512 values sit at
                // q = map(512 w + local p), a bit permutation (perm_in)
@@ -1091,7 +1127,8 @@ constexpr long long CONV_DIRECT_SMALL_POINTS = 1LL << 23;
 template<class C, In IN, Out OUT, Flt FLT> constexpr int resident_for()
 {
    return (((IN == In::C32 && OUT == Out::C32) || (IN == In::REAL2 && OUT == Out::REAL2)) &&
-           (FLT == Flt::BP_DIRECT || FLT == Flt::LIN_STAGED || FLT == Flt::R8_STAGED || FLT == Flt::R8BP_STAGED) &&
+           (FLT == Flt::BP_DIRECT || FLT == Flt::LIN_STAGED || FLT == Flt::R8_STAGED || FLT == Flt::R8BP_STAGED ||
+            FLT == Flt::R8BP_DIRECT) &&
            C::R == 16 && (C::N >= CONV_DIRECT_MIN_N || (FLT == Flt::BP_DIRECT && C::N == CONV_DIRECT_SMALL_N)))
              ? FUFFT_RESIDENT_THREADS_CONV_DIRECT
         : (IN == In::C32 && OUT == Out::C32 && C::H == 1 && C::R == 8 && C::N >= CONV_DIRECT_MIN_N)

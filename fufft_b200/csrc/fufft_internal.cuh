@@ -326,7 +326,7 @@ fufft_status launch_lin_staged(int n, const ConvArgs& a, cudaStream_t st, int de
 #define FUFFT_R8_ON_R16_LIN ((1 << 10) | (1 << 11) | (1 << 12))
 #endif
 #ifndef FUFFT_R8_ON_R16_BP
-#define FUFFT_R8_ON_R16_BP ((1 << 11) | (1 << 12))
+#define FUFFT_R8_ON_R16_BP ((1 << 10) | (1 << 11) | (1 << 12))
 #endif
 template<Mid MID, long long MASK, Flt FLT, In IN = In::C32, Out OUT = Out::C32>
 fufft_status launch_r8_on_r16(int n, const ConvArgs& a, cudaStream_t st, int dev)
@@ -342,6 +342,16 @@ fufft_status launch_r8_on_r16(int n, const ConvArgs& a, cudaStream_t st, int dev
 #undef FUFFT_PCASE
 }
 
+// the radix-8 register-boundary filter: read straight from global memory
+// (whole 32-byte sectors per four lanes) or staged per warp like the chain
+// order.  Interleaved A/B on B200 (1 GiB, % of HBM, direct / staged): 2048:
+// 83.3 / 77.3, 4096: 77.0 / 74.7; against the radix-8 engine at 1024: 81.8 /
+// 75.1 (512: 95.5 / 103.7, kept on radix 8)
+#ifndef FUFFT_R8BP_DIRECT
+#define FUFFT_R8BP_DIRECT 1
+#endif
+constexpr Flt R8BP_FLT = FUFFT_R8BP_DIRECT ? Flt::R8BP_DIRECT : Flt::R8BP_STAGED;
+
 // the two radix-8 layouts on the radix-16 engine, for one kernel family
 template<In IN, Out OUT, long long ML, long long MB>
 fufft_status dispatch_r8_on_r16(int n, fufft_midop mid, bool bperm, const ConvArgs& a, cudaStream_t st, int dev)
@@ -349,8 +359,8 @@ fufft_status dispatch_r8_on_r16(int n, fufft_midop mid, bool bperm, const ConvAr
    if(mid == FUFFT_MID_NONE || !in_mask(bperm ? MB : ML, n) || !aligned(a.b, 16) || (a.filter_stride * 8) % 16)
       return FUFFT_ERR_UNSUPPORTED;
    if(bperm)
-      return mid == FUFFT_MID_MULTIPLY ? launch_r8_on_r16<Mid::MUL, MB, Flt::R8BP_STAGED, IN, OUT>(n, a, st, dev)
-                                       : launch_r8_on_r16<Mid::CONJ, MB, Flt::R8BP_STAGED, IN, OUT>(n, a, st, dev);
+      return mid == FUFFT_MID_MULTIPLY ? launch_r8_on_r16<Mid::MUL, MB, R8BP_FLT, IN, OUT>(n, a, st, dev)
+                                       : launch_r8_on_r16<Mid::CONJ, MB, R8BP_FLT, IN, OUT>(n, a, st, dev);
    return mid == FUFFT_MID_MULTIPLY ? launch_r8_on_r16<Mid::MUL, ML, Flt::R8_STAGED, IN, OUT>(n, a, st, dev)
                                     : launch_r8_on_r16<Mid::CONJ, ML, Flt::R8_STAGED, IN, OUT>(n, a, st, dev);
 }

@@ -79,8 +79,8 @@ fufft_status family_conv2d_r8(int h, int w, fufft_midop mid, bool bperm, const C
    if(mid != FUFFT_MID_NONE && w >= 16 && in_mask(FUFFT_2D_R8_ON_R16, h * w) && aligned(a.b, 16) &&
       (a.filter_stride * 8) % 16 == 0) {
       const bool mul = mid == FUFFT_MID_MULTIPLY;
-      const fufft_status s = bperm ? (mul ? conv2d_on_r16<Mid::MUL, Flt::R8BP_STAGED>(h, w, a, st, dev)
-                                          : conv2d_on_r16<Mid::CONJ, Flt::R8BP_STAGED>(h, w, a, st, dev))
+      const fufft_status s = bperm ? (mul ? conv2d_on_r16<Mid::MUL, R8BP_FLT>(h, w, a, st, dev)
+                                          : conv2d_on_r16<Mid::CONJ, R8BP_FLT>(h, w, a, st, dev))
                                    : (mul ? conv2d_on_r16<Mid::MUL, Flt::R8_STAGED>(h, w, a, st, dev)
                                           : conv2d_on_r16<Mid::CONJ, Flt::R8_STAGED>(h, w, a, st, dev));
       if(s != FUFFT_ERR_UNSUPPORTED) return s;

@@ -5,7 +5,9 @@ the kernels do with them, and checks that every lane ends up holding, for each
 of its 16 chain positions, the value at the layout index that the oracle's own
 digit-reversal tables give for the same frequency -- for every 1-D size and
 2-D image shape the library sends down this path, in both radix-8 orders.  It
-also checks that no two values of a warp land in the same exchange slot."""
+also checks that no two values of a warp land in the same exchange slot, and
+that the direct read of the register-boundary order (lane part plus a
+constant per register) addresses the same indices in whole 32-byte sectors."""
 import json
 import os
 import shutil
@@ -39,7 +41,11 @@ template<class C, bool BP> void emit(int h, int w, bool& first)
    for(int i = 0; i < 8; ++i) printf("%s%d", i ? "," : "", T.s0[i]);
    printf("],\"s1\":[");
    for(int i = 0; i < 8; ++i) printf("%s%d", i ? "," : "", T.s1[i]);
-   printf("]}");
+   printf("],\"sig\":[");
+   for(int b = 0; b < PM::LB; ++b) printf("%s%d", b ? "," : "", T.sig[b]);
+   printf("],\"mapk\":[");
+   for(int k = 0; k < 16; ++k) printf("%s%d", k ? "," : "", T.mapk[k]);
+   printf("],\"cover\":%d}", PM::lanes_cover_q01() ? 1 : 0);
 }
 #define BOTH(H, W) emit<fufft::Chain2<H, W, 16>, false>(H, W, first); emit<fufft::Chain2<H, W, 16>, true>(H, W, first);
 int main()
@@ -125,3 +131,29 @@ def test_staging_tables_match_oracle_layouts(tables, oracle, shape, bp):
                 row = (8 * l + i) ^ (((8 * l + i) >> 3) & 7)
                 for half in (0, 1):
                     assert slots[2 * row + half] == want[16 * lane + 2 * i + half], (warp, l, i, half)
+
+
+@pytest.mark.parametrize("shape", [(1, n) for n in SHAPES_1D] + SHAPES_2D)
+def test_direct_register_boundary_read(tables, oracle, shape):
+    """Flt::R8BP_DIRECT: register k of `lane` reads index ql(lane) + map(k), and
+    each warp-wide load covers whole 32-byte sectors (four consecutive elements)"""
+    h, w = shape
+    n = h * w
+    tb = tables[(h, w, 1)]
+    if not tb["cover"]:
+        pytest.skip("this shape stages the register-boundary order instead")
+    want = _layout_index(oracle, h, w, 1)
+    lb = n.bit_length() - 1
+    sig = tb["sig"]
+    for lane in range(n // 16):
+        ql = sum(((lane >> t) & 1) << sig[4 + t] for t in range(lb - 4))
+        for k in range(16):
+            assert tb["mapk"][k] == sum(1 << sig[b] for b in range(4) if (k >> b) & 1)
+            assert ql + tb["mapk"][k] == want[16 * lane + k], (lane, k)
+    for warp in range(n // 16 // 32):
+        for k in range(16):
+            idx = [int(want[16 * (32 * warp + l) + k]) for l in range(32)]
+            sectors = {}
+            for q in idx:
+                sectors.setdefault(q // 4, set()).add(q % 4)
+            assert all(v == {0, 1, 2, 3} for v in sectors.values()), (warp, k)
