@@ -681,7 +681,7 @@ def run_ncu_all():
     call("conv fp32 R16_BPERM (register-boundary filter, read directly)", lambda: ops.conv(a, b, n, ops.LAYOUT_R16_BPERM, out=o), pts, 24 * pts)
     call("conv fp32 R16 (linear mixedrev16 filter, staged per warp)", lambda: ops.conv(a, b, n, ops.LAYOUT_R16, out=o),
          pts, 24 * pts)
-    call("conv fp32 R8_BPERM (radix-16 engine, filter staged through the bit permutation)",
+    call("conv fp32 R8_BPERM (radix-16 engine, filter read directly through the bit permutation)",
          lambda: ops.conv(a, b, n, ops.LAYOUT_R8_BPERM, out=o), pts, 24 * pts)
     call("conv fp32 R8 (linear mixedrev filter, radix-16 engine, bit-permutation staging)",
          lambda: ops.conv(a, b, n, ops.LAYOUT_R8, out=o), pts, 24 * pts)
